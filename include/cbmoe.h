@@ -1,0 +1,149 @@
+/* cbmoe: B200 (sm_100a) kernels for the codebook-quantized MoE expert path of the GLM engine in
+ * shallmall/kaggle-llm-endpoint. C ABI: plain pointers and sizes, no C++ or torch types.
+ *
+ * Conventions for every entry point:
+ *   - returns CBMOE_OK (0) or a negative CBMOE_ERR_* status; never throws, never aborts;
+ *   - pointer arguments are DEVICE pointers unless the name ends in _host;
+ *   - work is enqueued on `stream` (stream-ordered, asynchronous); nothing synchronizes unless documented;
+ *   - tables and buffers are owned by the caller; the library allocates no device memory on any path;
+ *   - bf16 tensors are passed as uint16_t bit patterns;
+ *   - kernels never trap: a device-side problem (a wait that ran out, an expert id out of range) sets a bit
+ *     that cbmoe_device_errors() reports.
+ * Reference paths below are relative to launcher/glm53-flash/engine/glm53/ in the reference repository.
+ */
+#ifndef CBMOE_H
+#define CBMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CBMOE_OK 0
+#define CBMOE_ERR_INVALID (-1)     /* bad argument: shape, alignment, null pointer */
+#define CBMOE_ERR_CUDA (-2)        /* a CUDA call failed: see cbmoe_last_cuda_error() */
+#define CBMOE_ERR_WORKSPACE (-3)   /* workspace smaller than the *_workspace_bytes() query */
+#define CBMOE_ERR_UNSUPPORTED (-4) /* valid request this build does not implement */
+#define CBMOE_ERR_NCCL (-5)        /* an NCCL call failed */
+#define CBMOE_ERR_DEVICE (-6)      /* a kernel recorded a device-side error (cbmoe_device_errors) */
+
+#define CBMOE_DEVERR_TIMEOUT 1     /* a bounded spin-wait gave up */
+#define CBMOE_DEVERR_INDEX 2       /* an expert id outside [0, E) was routed (the slot is skipped) */
+
+#define CBMOE_PATH_AUTO 0          /* decode kernel for small batches, grouped tensor-core GEMM otherwise */
+#define CBMOE_PATH_DECODE 1        /* fused dequant matvec (resident.py:110-120 `_apply_kernel`) */
+#define CBMOE_PATH_GROUPED 2       /* grouped dequant GEMM (resident.py:144-165 `_apply_ragged_kernel`) */
+
+/* ---------------------------------------------------------------------------------------------- library */
+int cbmoe_version(void);
+const char* cbmoe_status_string(int status);
+/* The cudaError_t of the last CBMOE_ERR_CUDA returned on this thread. */
+int cbmoe_last_cuda_error(void);
+/* Synchronizes the device, writes the OR of device error bits to *out_host, and clears them when clear != 0. */
+int cbmoe_device_errors(int clear, int* out_host);
+/* SM count of the current device (what the persistent kernels size their grids by). */
+int cbmoe_num_sms(void);
+/* Kernels this library has launched in this process (host-side counter). */
+long long cbmoe_launch_count(void);
+/* Per-kernel CUDA-event timing: when enabled, every launch is bracketed by two events on its stream.
+ * cbmoe_profile_read synchronizes on the recorded events and writes, per kernel kind (n_kinds >= 16 slots:
+ * 0 plan, 1 CB3 gate/up, 2 CB3 down, 3 CB3 single, 4 int8 gate/up, 5 int8 down+combine, 6 int8 single,
+ * 7 combine, 8 other), the summed milliseconds and launch counts; reset != 0 clears them. */
+int cbmoe_profile_enable(int enable);
+int cbmoe_profile_read(int reset, double* ms_host, long long* count_host, int n_kinds);
+
+/* ------------------------------------------------------------------------------------ CB3 kernel layout
+ * CB3 (benchmark format): per matrix W [rows, K], 3-bit indices packed little-endian into uint32 (index j at
+ * bits 3j..3j+2 of the row's bit stream, K*3/32 words per row) and one 8-entry bf16 codebook per row.
+ * The kernels read a load-time repack of it, "CB3K": the same 3 bits per weight and 16 bytes of codebook per
+ * row, reordered so that each lane of a decode warp reads its tensor-core fragment bits with 16-byte loads and
+ * every 256-input stage of a 64-row block is one contiguous bulk copy. nmat = 2 interleaves gate and up so one
+ * stage carries both. Requirements: rows % 64 == 0, K % 256 == 0.
+ * Replaces the load-time planar repack pack_chip_planes / planes.pack_planes (resident.py:48-60,
+ * planes.py:136-170). */
+size_t cbmoe_cb3k_idx_bytes(int E, int rows, int K, int nmat);
+size_t cbmoe_cb3k_cb_bytes(int E, int rows, int nmat);
+/* idx0/cb0 = matrix 0 (gate or the only matrix), idx1/cb1 = matrix 1 (up; NULL when nmat == 1):
+ * idx [E, rows, K*3/32] uint32, cb [E, rows, 8] bf16. Output idx_k / cb_k sized by the two queries. */
+int cbmoe_cb3k_repack(const uint32_t* idx0, const uint16_t* cb0, const uint32_t* idx1, const uint16_t* cb1,
+                      int nmat, int E, int rows, int K, void* idx_k, void* cb_k, cudaStream_t stream);
+/* Dequantize a CB3K table with the kernels' own register dequant -> bf16 [nmat, E, rows, K]
+ * (planes.dequant_planes, planes.py:196-291: the bit-exactness check of layout + dequant). */
+int cbmoe_cb3k_dequant(const void* idx_k, const void* cb_k, int nmat, int E, int rows, int K, uint16_t* out,
+                       cudaStream_t stream);
+
+/* ----------------------------------------------------------------------------------- int8 kernel layout
+ * int8 weight-only leaves as quant8.quantize_array makes them (quant8.py:26-32): q int8 [K_in, rows_out]
+ * ("[in, out]"), scales fp32 per output column (scale_axis 1, [rows_out]) or per input row (scale_axis 0,
+ * [K_in]). "W8K" is the same bytes transposed to output-row-major fragment order; nmat = 2 interleaves gate and
+ * up. Requirements: rows % 64 == 0, K % 256 == 0. */
+size_t cbmoe_w8k_bytes(int rows, int K, int nmat);
+int cbmoe_w8k_repack(const int8_t* q0, const int8_t* q1, int nmat, int K, int rows, void* qk, cudaStream_t stream);
+/* bf16(f32(q) * s) -> bf16 [nmat, rows, K] (quant8.dequant_tree, quant8.py:91-99), for the bit-exactness check. */
+int cbmoe_w8k_dequant(const void* qk, const float* s0, const float* s1, int scale_axis, int nmat, int rows, int K,
+                      uint16_t* out, cudaStream_t stream);
+
+/* --------------------------------------------------------------------------------------- routing plan
+ * pallas_moe.ragged_plan (pallas_moe.py:564-592) on the device: the T*k (token, slot) pairs sorted by expert
+ * (stable) into tm-row blocks, plus the lists the decode kernels walk. All int32 except w_row (fp32).
+ * Layout of the plan buffer, offsets in 4-byte words from cbmoe_plan_layout (index: field):
+ *   0 counts[E]  1 row_start[E] (first sorted row of each expert)  2 act[E] (active experts, ascending)
+ *   3 n_act[1]  4 n_blocks[1]  5 n_pass[1]  6 blk_expert[G]  7 tok_row[Rp] (-1 = padding)  8 w_row[Rp]
+ *   9 row_slot[T*k]  10 pass_expert[P]  11 pass_row0[P]  12 pass_cnt[P]  13 total words
+ * G = ceil(T*k/tm) + E, Rp = G*tm, P = ceil(T*k/pass_tokens) + E. A "pass" is up to pass_tokens consecutive
+ * sorted rows of one expert: the decode kernels stream an expert's weights once per pass. */
+int cbmoe_plan_layout(int T, int k, int E, int tm, int pass_tokens, int64_t* offsets14_host);
+int cbmoe_route_plan(const int32_t* idx, const float* w, int T, int k, int E, int tm, int pass_tokens, void* plan,
+                     size_t plan_bytes, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------------------------ the layer */
+typedef struct cbmoe_experts {
+  int E, H, I;                 /* routed experts, hidden size, expert intermediate size */
+  const void* gateup_idx;      /* CB3K nmat = 2 (gate, up), rows = I, K = H */
+  const void* gateup_cb;
+  const void* down_idx;        /* CB3K nmat = 1, rows = H, K = I */
+  const void* down_cb;
+} cbmoe_experts;
+
+typedef struct cbmoe_shared {
+  const void* gateup_q;        /* W8K nmat = 2 (gate, up), rows = I, K = H */
+  const float* gate_s;
+  const float* up_s;
+  const void* down_q;          /* W8K nmat = 1, rows = H, K = I */
+  const float* down_s;
+  int scale_axis;              /* 1: per output channel (benchmark configs), 0: per input row */
+} cbmoe_shared;
+
+/* Workspace bytes for cbmoe_experts_apply / cbmoe_moe_layer with N tokens and top-k routing. */
+size_t cbmoe_workspace_bytes(const cbmoe_experts* ex, int N, int k, int path);
+
+/* ResidentFetch.apply (resident.py:100-108): x bf16 [N, H], idx int32 [N, k] in [0, E), w fp32 [N, k] ->
+ * y fp32 [N, H] = sum_j w[n, j] * down_e(swiglu_clamped(gate_e x_n, up_e x_n, limit)), e = idx[n, j]. */
+int cbmoe_experts_apply(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx, const float* w,
+                        int k, float limit, int path, float* y, void* workspace, size_t workspace_bytes,
+                        cudaStream_t stream);
+
+/* moe_dense below the router (model.py:840-856): routed experts + int8 shared expert (model.py:125-127),
+ * out bf16 [N, H]. */
+int cbmoe_moe_layer(const cbmoe_experts* ex, const cbmoe_shared* sh, const uint16_t* x, int N, const int32_t* idx,
+                    const float* w, int k, float limit, int path, uint16_t* out, void* workspace,
+                    size_t workspace_bytes, cudaStream_t stream);
+
+/* One CB3K matrix times N activation rows (pallas_moe.moe_matvec with every slot on expert 0,
+ * pallas_moe.py:238-307): x bf16 [N, K] -> y fp32 [N, rows]. Workspace: cbmoe_matvec_workspace_bytes. */
+size_t cbmoe_matvec_workspace_bytes(int N);
+int cbmoe_cb3_matvec(const void* idx_k, const void* cb_k, int rows, int K, const uint16_t* x, int N, float* y,
+                     void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* int8 weight-only linear (quant8.dequant_tree + the consuming dot, quant8.py:91-99): x bf16 [N, K] ->
+ * y fp32 [N, rows] = x @ bf16(q * s). Workspace: cbmoe_matvec_workspace_bytes. */
+int cbmoe_w8_linear(const void* qk, const float* s, int scale_axis, int rows, int K, const uint16_t* x, int N,
+                    float* y, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CBMOE_H */

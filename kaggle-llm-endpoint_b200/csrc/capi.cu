@@ -1,0 +1,292 @@
+// C-ABI entry points of the expert layer (include/cbmoe.h): argument checks, workspace carving and the kernel
+// sequence of one call. The drop-in boundary is ResidentFetch.apply (resident.py:100-108) and moe_dense below the
+// router (model.py:840-856).
+#include <cstdio>
+
+#include "decode.cuh"
+
+namespace cbmoe {
+
+__device__ int g_device_errors = 0;
+
+namespace {
+thread_local int t_last_cuda_error = 0;
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t v) { return (v + kAlign - 1) & ~(kAlign - 1); }
+
+struct PlanLayoutHost {
+  int64_t off[14];
+};
+
+PlanLayoutHost host_plan_layout(int T, int k, int E, int tm, int pass_tokens) {
+  PlanLayoutHost L;
+  cbmoe_plan_layout(T, k, E, tm, pass_tokens, L.off);
+  return L;
+}
+
+// Tokens per expert pass of the decode kernels for a batch of N tokens (each token picks an expert at most once).
+int decode_nt(int N) { return N <= 8 ? 1 : (N <= 16 ? 2 : 4); }
+
+// Workspace of the decode path: [plan | h (Rp x 2I bf16) | y_sorted (Rp x H f32) | h_shared (N x 2I bf16)].
+struct DecodeWorkspace {
+  size_t plan, h, y, hs, total;
+  int nt, Rp;
+  PlanLayoutHost L;
+};
+
+DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k) {
+  DecodeWorkspace w;
+  w.nt = decode_nt(N);
+  w.L = host_plan_layout(N, k, E, 1, 8 * w.nt);
+  w.Rp = (int)(w.L.off[8] - w.L.off[7]);
+  w.plan = 0;
+  w.h = align_up((size_t)w.L.off[13] * 4);
+  w.y = w.h + align_up((size_t)w.Rp * 2 * I * 2);
+  w.hs = w.y + align_up((size_t)w.Rp * H * 4);
+  w.total = w.hs + align_up((size_t)N * 2 * I * 2);
+  return w;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+bool experts_ok(const cbmoe_experts* ex) {
+  return ex && ex->E > 0 && ex->E <= 1024 && ex->H > 0 && ex->I > 0 && ex->H % kStageK == 0 &&
+         ex->I % kStageK == 0 && ex->gateup_idx && ex->gateup_cb && ex->down_idx && ex->down_cb &&
+         aligned16(ex->gateup_idx) && aligned16(ex->down_idx) && aligned16(ex->gateup_cb) && aligned16(ex->down_cb);
+}
+
+bool shared_ok(const cbmoe_shared* sh) {
+  return sh && sh->gateup_q && sh->gate_s && sh->up_s && sh->down_q && sh->down_s &&
+         (sh->scale_axis == 0 || sh->scale_axis == 1) && aligned16(sh->gateup_q) && aligned16(sh->down_q);
+}
+
+DecodeParams base_params() {
+  DecodeParams p{};
+  p.E = 1;
+  p.topk = 1;
+  return p;
+}
+
+// Plan + routed gate/up + routed down into the workspace; returns the plan pointer through *plan_out.
+int routed_decode(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx, const float* w, int k,
+                  float limit, uint8_t* ws, const DecodeWorkspace& W, cudaStream_t stream) {
+  int32_t* plan = reinterpret_cast<int32_t*>(ws + W.plan);
+  int rc = launch_route_plan(idx, w, N, k, ex->E, 1, 8 * W.nt, plan, stream);
+  if (rc) return rc;
+  uint16_t* h = reinterpret_cast<uint16_t*>(ws + W.h);
+  float* ys = reinterpret_cast<float*>(ws + W.y);
+
+  DecodeParams p = base_params();
+  p.wq = static_cast<const uint8_t*>(ex->gateup_idx);
+  p.cb = static_cast<const uint32_t*>(ex->gateup_cb);
+  p.rows = ex->I;
+  p.K = ex->H;
+  p.RB = ex->I / kRowsPerBlock;
+  p.KS = ex->H / kStageK;
+  p.b = x;
+  p.b_hilo = 0;
+  p.tok_row = plan + W.L.off[7];
+  p.pass_expert = plan + W.L.off[10];
+  p.pass_row0 = plan + W.L.off[11];
+  p.pass_cnt = plan + W.L.off[12];
+  p.n_pass = plan + W.L.off[5];
+  p.N = N;
+  p.E = ex->E;
+  p.limit = limit;
+  p.h_out = h;
+  rc = decode_cb3_gateup(p, W.nt, stream);
+  if (rc) return rc;
+
+  DecodeParams d = p;
+  d.wq = static_cast<const uint8_t*>(ex->down_idx);
+  d.cb = static_cast<const uint32_t*>(ex->down_cb);
+  d.rows = ex->H;
+  d.K = ex->I;
+  d.RB = ex->H / kRowsPerBlock;
+  d.KS = ex->I / kStageK;
+  d.b = h;
+  d.b_hilo = 1;
+  d.tok_row = nullptr;
+  d.h_out = nullptr;
+  d.y_out = ys;
+  return decode_cb3_down(d, W.nt, stream);
+}
+
+}  // namespace
+
+void set_last_cuda_error(cudaError_t e) { t_last_cuda_error = (int)e; }
+
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+}  // namespace cbmoe
+
+using namespace cbmoe;
+
+extern "C" int cbmoe_version(void) { return 1; }
+
+extern "C" const char* cbmoe_status_string(int status) {
+  switch (status) {
+    case CBMOE_OK: return "ok";
+    case CBMOE_ERR_INVALID: return "invalid argument";
+    case CBMOE_ERR_CUDA: return "CUDA error";
+    case CBMOE_ERR_WORKSPACE: return "workspace too small";
+    case CBMOE_ERR_UNSUPPORTED: return "unsupported";
+    case CBMOE_ERR_NCCL: return "NCCL error";
+    case CBMOE_ERR_DEVICE: return "device-side error";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int cbmoe_last_cuda_error(void) { return t_last_cuda_error; }
+
+extern "C" int cbmoe_num_sms(void) { return num_sms(); }
+
+extern "C" int cbmoe_device_errors(int clear, int* out_host) {
+  if (!out_host) return CBMOE_ERR_INVALID;
+  CBMOE_CUDA_TRY(cudaDeviceSynchronize());
+  int v = 0;
+  CBMOE_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_device_errors, sizeof(int)));
+  *out_host = v;
+  if (clear) {
+    const int zero = 0;
+    CBMOE_CUDA_TRY(cudaMemcpyToSymbol(g_device_errors, &zero, sizeof(int)));
+  }
+  return CBMOE_OK;
+}
+
+extern "C" size_t cbmoe_workspace_bytes(const cbmoe_experts* ex, int N, int k, int path) {
+  if (!ex || N < 0 || k <= 0 || ex->E <= 0) return 0;
+  (void)path;
+  return decode_workspace(ex->E, ex->H, ex->I, N, k).total;
+}
+
+static int check_common(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx, const float* w,
+                        int k, int path) {
+  if (!experts_ok(ex) || N < 0 || k <= 0 || k > 64) return CBMOE_ERR_INVALID;
+  if (N > 0 && (!x || !idx || !w || !aligned16(x))) return CBMOE_ERR_INVALID;
+  if (path != CBMOE_PATH_AUTO && path != CBMOE_PATH_DECODE && path != CBMOE_PATH_GROUPED) return CBMOE_ERR_INVALID;
+  if (path == CBMOE_PATH_GROUPED) return CBMOE_ERR_UNSUPPORTED;
+  return CBMOE_OK;
+}
+
+extern "C" int cbmoe_experts_apply(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx,
+                                   const float* w, int k, float limit, int path, float* y, void* workspace,
+                                   size_t workspace_bytes, cudaStream_t stream) {
+  int rc = check_common(ex, x, N, idx, w, k, path);
+  if (rc) return rc;
+  if (N > 0 && !y) return CBMOE_ERR_INVALID;
+  if (N == 0) return CBMOE_OK;
+  const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k);
+  if (!workspace || workspace_bytes < W.total) return CBMOE_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  rc = routed_decode(ex, x, N, idx, w, k, limit, ws, W, stream);
+  if (rc) return rc;
+  const int32_t* plan = reinterpret_cast<const int32_t*>(ws + W.plan);
+  return launch_combine(reinterpret_cast<const float*>(ws + W.y), plan + W.L.off[9], w, N, k, ex->H, y, stream);
+}
+
+extern "C" int cbmoe_moe_layer(const cbmoe_experts* ex, const cbmoe_shared* sh, const uint16_t* x, int N,
+                               const int32_t* idx, const float* w, int k, float limit, int path, uint16_t* out,
+                               void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  int rc = check_common(ex, x, N, idx, w, k, path);
+  if (rc) return rc;
+  if (!shared_ok(sh) || (N > 0 && !out)) return CBMOE_ERR_INVALID;
+  if (N == 0) return CBMOE_OK;
+  const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k);
+  if (!workspace || workspace_bytes < W.total) return CBMOE_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  rc = routed_decode(ex, x, N, idx, w, k, limit, ws, W, stream);
+  if (rc) return rc;
+  const int32_t* plan = reinterpret_cast<const int32_t*>(ws + W.plan);
+  uint16_t* hs = reinterpret_cast<uint16_t*>(ws + W.hs);
+
+  DecodeParams p = base_params();
+  p.wq = static_cast<const uint8_t*>(sh->gateup_q);
+  p.s0 = sh->gate_s;
+  p.s1 = sh->up_s;
+  p.scale_axis = sh->scale_axis;
+  p.rows = ex->I;
+  p.K = ex->H;
+  p.RB = ex->I / kRowsPerBlock;
+  p.KS = ex->H / kStageK;
+  p.b = x;
+  p.N = N;
+  p.limit = limit;
+  p.h_out = hs;
+  rc = decode_w8_gateup(p, decode_nt(N), stream);
+  if (rc) return rc;
+
+  DecodeParams d = base_params();
+  d.wq = static_cast<const uint8_t*>(sh->down_q);
+  d.s0 = sh->down_s;
+  d.scale_axis = sh->scale_axis;
+  d.rows = ex->H;
+  d.K = ex->I;
+  d.RB = ex->H / kRowsPerBlock;
+  d.KS = ex->I / kStageK;
+  d.b = hs;
+  d.b_hilo = 1;
+  d.N = N;
+  d.y_sorted = reinterpret_cast<const float*>(ws + W.y);
+  d.row_slot = plan + W.L.off[9];
+  d.wts = w;
+  d.topk = k;
+  d.out_bf16 = out;
+  return decode_w8_down_combine(d, decode_nt(N), stream);
+}
+
+extern "C" size_t cbmoe_matvec_workspace_bytes(int N) { return N >= 0 ? 0 : 0; }
+
+extern "C" int cbmoe_cb3_matvec(const void* idx_k, const void* cb_k, int rows, int K, const uint16_t* x, int N,
+                                float* y, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  if (!idx_k || !cb_k || rows <= 0 || K <= 0 || rows % kRowsPerBlock || K % kStageK || N < 0) return CBMOE_ERR_INVALID;
+  if (N > 0 && (!x || !y || !aligned16(x) || !aligned16(idx_k) || !aligned16(cb_k))) return CBMOE_ERR_INVALID;
+  if (N == 0) return CBMOE_OK;
+  DecodeParams p = base_params();
+  p.wq = static_cast<const uint8_t*>(idx_k);
+  p.cb = static_cast<const uint32_t*>(cb_k);
+  p.rows = rows;
+  p.K = K;
+  p.RB = rows / kRowsPerBlock;
+  p.KS = K / kStageK;
+  p.b = x;
+  p.N = N;
+  p.y_out = y;
+  return decode_cb3_single(p, decode_nt(N), stream);
+}
+
+extern "C" int cbmoe_w8_linear(const void* qk, const float* s, int scale_axis, int rows, int K, const uint16_t* x,
+                               int N, float* y, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  if (!qk || !s || rows <= 0 || K <= 0 || rows % kRowsPerBlock || K % kStageK || N < 0 ||
+      (scale_axis != 0 && scale_axis != 1))
+    return CBMOE_ERR_INVALID;
+  if (N > 0 && (!x || !y || !aligned16(x) || !aligned16(qk))) return CBMOE_ERR_INVALID;
+  if (N == 0) return CBMOE_OK;
+  DecodeParams p = base_params();
+  p.wq = static_cast<const uint8_t*>(qk);
+  p.s0 = s;
+  p.scale_axis = scale_axis;
+  p.rows = rows;
+  p.K = K;
+  p.RB = rows / kRowsPerBlock;
+  p.KS = K / kStageK;
+  p.b = x;
+  p.N = N;
+  p.y_out = y;
+  return decode_w8_single(p, decode_nt(N), stream);
+}

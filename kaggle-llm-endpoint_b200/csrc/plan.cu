@@ -1,0 +1,244 @@
+// Device routing plan: pallas_moe.ragged_plan (pallas_moe.py:564-592) plus the per-expert pass lists the decode
+// kernels walk. One CTA: a stable counting sort of the T*k (token, slot) pairs by expert.
+//   pass A  each warp counts its contiguous slot range per expert (warp match_any, no atomics)
+//   scan    per-expert totals -> padded row starts, block starts, pass starts, active list (warp scans)
+//   pass C  each warp re-walks its range; a slot's sorted row = its expert's row start + the slots of that expert
+//           in earlier warps + earlier slots in this warp: the same order as a stable argsort.
+#include "common.cuh"
+#include "profile.cuh"
+
+namespace cbmoe {
+
+constexpr int kPlanWarps = 16;
+constexpr int kPlanThreads = kPlanWarps * 32;
+constexpr int kPlanMaxExperts = 1024;
+
+struct PlanLayout {
+  int64_t off[14];
+};
+
+__host__ __device__ inline PlanLayout plan_layout(int T, int k, int E, int tm, int pass_tokens) {
+  const int64_t S = (int64_t)T * k;
+  const int64_t G = (S + tm - 1) / tm + E;
+  const int64_t Rp = G * tm;
+  const int64_t P = (S + pass_tokens - 1) / pass_tokens + E;
+  auto up4 = [](int64_t v) { return (v + 3) & ~int64_t(3); };
+  PlanLayout L;
+  L.off[0] = 0;
+  L.off[1] = up4(E);
+  L.off[2] = L.off[1] + up4(E);
+  L.off[3] = L.off[2] + up4(E);
+  L.off[4] = L.off[3] + 1;
+  L.off[5] = L.off[4] + 1;
+  L.off[6] = up4(L.off[5] + 1);
+  L.off[7] = L.off[6] + up4(G);
+  L.off[8] = L.off[7] + up4(Rp);
+  L.off[9] = L.off[8] + up4(Rp);
+  L.off[10] = L.off[9] + up4(S);
+  L.off[11] = L.off[10] + up4(P);
+  L.off[12] = L.off[11] + up4(P);
+  L.off[13] = L.off[12] + up4(P);
+  return L;
+}
+
+namespace {
+
+// Exclusive warp scan of v; returns the prefix and writes the warp total to *total.
+__device__ __forceinline__ int warp_exclusive_scan(int v, int* total) {
+  const int lane = threadIdx.x & 31;
+  int x = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, d);
+    if (lane >= d) x += y;
+  }
+  *total = __shfl_sync(0xffffffffu, x, 31);
+  return x - v;
+}
+
+__global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(const int32_t* __restrict__ idx,
+                                                                  const float* __restrict__ wts, int T, int k, int E,
+                                                                  int tm, int pass_tokens, int32_t* __restrict__ plan,
+                                                                  PlanLayout L) {
+  extern __shared__ int sm[];
+  int* cnt = sm;                               // [kPlanWarps][E]
+  int* counts = cnt + kPlanWarps * E;          // [E]
+  int* ends = counts + E;                      // [E] block end (exclusive) per expert
+  __shared__ int s_tot[4];
+
+  const int S = T * k;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int per_warp = ((S + kPlanWarps - 1) / kPlanWarps + 31) & ~31;
+  const int beg = warp * per_warp;
+  const int end = min(S, beg + per_warp);
+
+  for (int i = threadIdx.x; i < kPlanWarps * E; i += kPlanThreads) cnt[i] = 0;
+  __syncthreads();
+
+  // pass A: per-warp per-expert counts
+  for (int base = beg; base < end; base += 32) {
+    const int s = base + lane;
+    int e = (s < end) ? idx[s] : -1;
+    if (s < end && (e < 0 || e >= E)) {
+      atomicOr(&g_device_errors, CBMOE_DEVERR_INDEX);
+      e = -1;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * E + e] += __popc(peers);
+  }
+  __syncthreads();
+
+  int32_t* counts_g = plan + L.off[0];
+  int32_t* row_start = plan + L.off[1];
+  int32_t* act = plan + L.off[2];
+  int32_t* pass_expert = plan + L.off[10];
+  int32_t* pass_row0 = plan + L.off[11];
+  int32_t* pass_cnt = plan + L.off[12];
+  const int P = (int)(L.off[11] - L.off[10]);
+
+  for (int e = threadIdx.x; e < E; e += kPlanThreads) {
+    int c = 0;
+    for (int w = 0; w < kPlanWarps; ++w) c += cnt[w * E + e];
+    counts[e] = c;
+  }
+  __syncthreads();
+
+  // scans over experts (warp 0), 32 experts per step
+  if (warp == 0) {
+    int run_rows = 0, run_blocks = 0, run_pass = 0, run_act = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const int c = (e < E) ? counts[e] : 0;
+      const int nb = (c + tm - 1) / tm;
+      const int np = (c + pass_tokens - 1) / pass_tokens;
+      int t_rows, t_blocks, t_pass, t_act;
+      const int x_rows = warp_exclusive_scan(nb * tm, &t_rows);
+      const int x_blocks = warp_exclusive_scan(nb, &t_blocks);
+      const int x_pass = warp_exclusive_scan(np, &t_pass);
+      const int x_act = warp_exclusive_scan(c > 0 ? 1 : 0, &t_act);
+      if (e < E) {
+        const int rs = run_rows + x_rows;
+        counts_g[e] = c;
+        row_start[e] = rs;
+        ends[e] = run_blocks + x_blocks + nb;
+        if (c > 0) act[run_act + x_act] = e;
+        for (int p = 0; p < np; ++p) {
+          const int q = run_pass + x_pass + p;
+          pass_expert[q] = e;
+          pass_row0[q] = rs + p * pass_tokens;
+          pass_cnt[q] = min(pass_tokens, c - p * pass_tokens);
+        }
+        // turn this expert's per-warp counts into per-warp starting rows
+        int run = rs;
+        for (int w = 0; w < kPlanWarps; ++w) {
+          const int v = cnt[w * E + e];
+          cnt[w * E + e] = run;
+          run += v;
+        }
+      }
+      run_rows += t_rows;
+      run_blocks += t_blocks;
+      run_pass += t_pass;
+      run_act += t_act;
+    }
+    if (lane == 0) {
+      s_tot[0] = run_act;
+      s_tot[1] = run_blocks;
+      s_tot[2] = run_pass;
+      plan[L.off[3]] = run_act;
+      plan[L.off[4]] = run_blocks;
+      plan[L.off[5]] = run_pass;
+    }
+  }
+  // padding rows and unused list entries
+  const int Rp = (int)(L.off[8] - L.off[7]);
+  int32_t* tok_row = plan + L.off[7];
+  float* w_row = reinterpret_cast<float*>(plan + L.off[8]);
+  for (int r = threadIdx.x; r < Rp; r += kPlanThreads) {
+    tok_row[r] = -1;
+    w_row[r] = 0.f;
+  }
+  __syncthreads();
+  for (int i = s_tot[0] + threadIdx.x; i < E; i += kPlanThreads) act[i] = -1;
+  for (int i = s_tot[2] + threadIdx.x; i < P; i += kPlanThreads) {
+    pass_expert[i] = -1;
+    pass_row0[i] = 0;
+    pass_cnt[i] = 0;
+  }
+
+  // pass C: stable placement
+  int32_t* row_slot = plan + L.off[9];
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int base = beg; base < end; base += 32) {
+    const int s = base + lane;
+    int e = (s < end) ? idx[s] : -1;
+    if (e >= E) e = -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    int pos = -1;
+    if (e >= 0) {
+      pos = cnt[warp * E + e] + __popc(peers & lt_mask);
+      tok_row[pos] = s / k;
+      w_row[pos] = wts[s];
+    }
+    if (s < end) row_slot[s] = pos;
+    __syncwarp();
+    if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * E + e] += __popc(peers);
+    __syncwarp();
+  }
+
+  // block -> expert (first expert whose block range ends after the block; blocks past n_blocks repeat the last)
+  const int G = (int)(L.off[7] - L.off[6]);
+  int32_t* blk_expert = plan + L.off[6];
+  const int n_blocks = s_tot[1];
+  auto find = [&](int g) {
+    int lo = 0, hi = E;  // first e with ends[e] > g
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (ends[mid] > g) hi = mid; else lo = mid + 1;
+    }
+    return min(lo, E - 1);
+  };
+  const int last = find(max(n_blocks - 1, 0));
+  for (int g = threadIdx.x; g < G; g += kPlanThreads) blk_expert[g] = (g < n_blocks) ? find(g) : last;
+}
+
+}  // namespace
+
+size_t plan_smem_bytes(int E) { return (size_t)(kPlanWarps + 2) * E * sizeof(int); }
+
+int launch_route_plan(const int32_t* idx, const float* w, int T, int k, int E, int tm, int pass_tokens,
+                      int32_t* plan, cudaStream_t stream) {
+  const PlanLayout L = plan_layout(T, k, E, tm, pass_tokens);
+  const size_t smem = plan_smem_bytes(E);
+  static bool attr_set = false;
+  if (!attr_set) {
+    CBMOE_CUDA_TRY(cudaFuncSetAttribute(route_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)plan_smem_bytes(kPlanMaxExperts)));
+    attr_set = true;
+  }
+  prof_begin(kProfPlan, stream);
+  route_plan_kernel<<<1, kPlanThreads, smem, stream>>>(idx, w, T, k, E, tm, pass_tokens, plan, L);
+  prof_end(kProfPlan, stream);
+  CBMOE_CUDA_TRY(cudaGetLastError());
+  return CBMOE_OK;
+}
+
+}  // namespace cbmoe
+
+extern "C" int cbmoe_plan_layout(int T, int k, int E, int tm, int pass_tokens, int64_t* offsets14_host) {
+  if (T < 0 || k <= 0 || E <= 0 || E > cbmoe::kPlanMaxExperts || tm <= 0 || pass_tokens <= 0 || !offsets14_host)
+    return CBMOE_ERR_INVALID;
+  const cbmoe::PlanLayout L = cbmoe::plan_layout(T, k, E, tm, pass_tokens);
+  for (int i = 0; i < 14; ++i) offsets14_host[i] = L.off[i];
+  return CBMOE_OK;
+}
+
+extern "C" int cbmoe_route_plan(const int32_t* idx, const float* w, int T, int k, int E, int tm, int pass_tokens,
+                                void* plan, size_t plan_bytes, cudaStream_t stream) {
+  if (T < 0 || k <= 0 || E <= 0 || E > cbmoe::kPlanMaxExperts || tm <= 0 || pass_tokens <= 0 || !plan ||
+      (T > 0 && (!idx || !w)))
+    return CBMOE_ERR_INVALID;
+  const cbmoe::PlanLayout L = cbmoe::plan_layout(T, k, E, tm, pass_tokens);
+  if (plan_bytes < (size_t)L.off[13] * 4) return CBMOE_ERR_WORKSPACE;
+  return cbmoe::launch_route_plan(idx, w, T, k, E, tm, pass_tokens, static_cast<int32_t*>(plan), stream);
+}

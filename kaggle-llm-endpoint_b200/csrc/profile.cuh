@@ -1,0 +1,25 @@
+// Kernel kinds for launch accounting and per-kernel event timing (profile.cu, cbmoe_profile_read).
+#pragma once
+#include <cuda_runtime.h>
+
+#include "../../include/cbmoe.h"
+
+namespace cbmoe {
+
+enum ProfKind {
+  kProfPlan = 0,          // route_plan_kernel
+  kProfCb3GateUp = 1,     // decode_kernel_t<CB3, 2 matrices, SWIGLU>
+  kProfCb3Down = 2,       // decode_kernel_t<CB3, 1 matrix, STORE, hi/lo B>
+  kProfCb3Single = 3,     // decode_kernel_t<CB3, 1 matrix, STORE>
+  kProfW8GateUp = 4,      // decode_kernel_t<W8, 2 matrices, SWIGLU>
+  kProfW8DownCombine = 5, // decode_kernel_t<W8, 1 matrix, COMBINE>
+  kProfW8Single = 6,      // decode_kernel_t<W8, 1 matrix, STORE>
+  kProfCombine = 7,       // combine_kernel
+  kProfOther = 8,         // layout repacks and dequant checks
+  kProfKinds = 16
+};
+
+void prof_begin(int kind, cudaStream_t s);
+void prof_end(int kind, cudaStream_t s);
+
+}  // namespace cbmoe

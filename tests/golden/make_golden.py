@@ -164,7 +164,7 @@ def gen_compositions():
     swiglu = ref_function("model.py", "swiglu_clamped", extra={"silu": silu})
     ragged_plan = ref_function("pallas_moe.py", "ragged_plan")
     rng = np.random.default_rng(14)
-    E, H, I = 6, 64, 32
+    E, H, I = 6, 256, 256        # kernel granularity: rows % 64 == 0, inputs % 256 == 0
 
     def deq(tbl):
         idx, cb = tbl

@@ -1,0 +1,67 @@
+"""The C-ABI library loads without a GPU and exports every function include/*.h declares; host-side argument
+checks reject bad calls before touching the device. No GPU: nothing here launches a kernel."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+DECL = re.compile(r"^\s*(?:const\s+)?(?:long\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\*?\s*(cbmoe_[A-Za-z0-9_]+)\s*\(", re.M)
+
+
+def declared():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        names |= set(DECL.findall(open(h).read()))
+    return sorted(names)
+
+
+@pytest.fixture(scope="module")
+def L():
+    import cbmoe
+    return cbmoe.lib()
+
+
+def test_header_declares_the_layer_api():
+    names = declared()
+    for n in ("cbmoe_experts_apply", "cbmoe_moe_layer", "cbmoe_route_plan", "cbmoe_cb3k_repack", "cbmoe_w8k_repack",
+              "cbmoe_cb3_matvec", "cbmoe_w8_linear"):
+        assert n in names
+
+
+def test_every_declared_symbol_is_exported(L):
+    missing = [n for n in declared() if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_every_symbol():
+    from cbmoe._lib import SIGNATURES
+    assert sorted(SIGNATURES) == declared()
+
+
+def test_host_side_checks_without_gpu(L):
+    from cbmoe._lib import Experts
+    assert L.cbmoe_version() >= 1
+    assert L.cbmoe_status_string(-1) == b"invalid argument"
+    # bad shapes never reach a kernel
+    assert L.cbmoe_cb3k_idx_bytes(160, 1536, 5120, 2) == 160 * 1536 * 5120 * 2 * 3 // 8
+    assert L.cbmoe_cb3k_cb_bytes(160, 1536, 2) == 160 * 1536 * 2 * 16
+    assert L.cbmoe_w8k_bytes(1536, 5120, 2) == 1536 * 5120 * 2
+    assert L.cbmoe_cb3k_repack(None, None, None, None, 1, 1, 100, 256, None, None, None) == -1   # rows % 64
+    assert L.cbmoe_cb3k_repack(None, None, None, None, 1, 1, 64, 100, None, None, None) == -1    # K % 256
+    ex = Experts(0, 5120, 1536, None, None, None, None)
+    assert L.cbmoe_experts_apply(ctypes.byref(ex), None, 8, None, None, 8, 10.0, 0, None, None, 0, None) == -1
+    ex = Experts(160, 5120, 1536, 16, 16, 16, 16)
+    assert L.cbmoe_experts_apply(ctypes.byref(ex), None, 8, None, None, 8, 10.0, 0, None, None, 0, None) == -1
+    assert L.cbmoe_experts_apply(ctypes.byref(ex), 16, 8, 16, 16, 8, 10.0, 0, 16, None, 0, None) == -3   # workspace
+
+
+def test_plan_layout_sizes(L):
+    off = (ctypes.c_int64 * 14)()
+    assert L.cbmoe_plan_layout(4096, 8, 160, 128, 32, off) == 0
+    S, E, tm = 4096 * 8, 160, 128
+    G = -(-S // tm) + E
+    assert off[7] - off[6] >= G and off[8] - off[7] >= G * tm and off[10] - off[9] >= S
+    assert L.cbmoe_plan_layout(8, 8, 2048, 1, 8, off) == -1      # more experts than the plan kernel supports
