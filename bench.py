@@ -1,0 +1,442 @@
+"""Benchmark of the codebook-MoE decode layer (the benchmark's config 1) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (config 1): one GLM-style MoE layer in decode: hidden 5120, 160 routed experts in the 3-bit CB3 codebook
+format (uniform indices, sorted N(0, 0.02) bf16 codebooks per row) + 1 shared expert in int8 with per-output-channel
+fp32 scales, intermediate 1536, SwiGLU (limit 10), 8 tokens of N(0, 1) bf16 activations, top-8 softmax routing of
+N(0, 1) logits. Synthetic data generated on the GPU from fixed seeds (no checkpoint exists for this format).
+
+A step = one layer call (routing plan, routed gate/up + SwiGLU, routed down, shared gate/up, shared down + the
+weighted combine) on one batch. Steps cycle through 16 resident layers (1.47 GB of weights each, 23.5 GB total) and
+64 routing batches, so every step streams ~0.5 GB of weights that the previous step did not touch: inputs larger
+than the 126 MB L2, no flush needed.
+
+JSON line (rank 0): value = tokens/s with inputs resident in HBM (CUDA events over exactly K steps, max over
+ranks); e2e = the same through the public API with pinned host inputs copied in and the bf16 output copied out
+every step; roofline = the dominant kernel's algorithmic bytes / its event-timed duration vs the measured HBM copy
+peak; cpu_baseline = the C oracle (OpenMP) on a bounded sample of the same workload on this host's cores.
+--impl reference times that CPU restatement alone (the reference's own path is JAX-on-TPU and cannot run here).
+N > 1: every rank runs the same workload on its own GPU as an independent replica (scaling "weak").
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "kaggle-llm-endpoint_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "MoE-layer tok/s & dequant-matvec HBM GB/s (% of peak) at 1/2/4/8 B200"
+H, I, E, TOPK, N_TOK, LIMIT = 5120, 1536, 160, 8, 8, 10.0
+N_LAYERS, N_BATCHES = 16, 64
+FALLBACK_HBM_GBS = 6650.0
+CB3_EXPERT_BYTES = 3 * I * H * 3 // 8 + (2 * I + H) * 16          # 8,978,432
+SHARED_BYTES = 3 * H * I + (2 * I + H) * 4                          # 23,625,728 (int8 + fp32 scales)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
+    ap.add_argument("--layers", type=int, default=N_LAYERS, help="resident layers cycled by the steps (profiling "
+                    "captures use 1 to keep device memory small)")
+    return ap.parse_args()
+
+
+def config_block(n_gpus):
+    return {"workload": "config1: MoE decode layer, 8 tokens, E=160 CB3 routed + int8 shared, H=5120, I=1536, top-8",
+            "global_batch": N_TOK * n_gpus, "tokens_per_gpu": N_TOK, "hidden": H, "experts": E, "intermediate": I,
+            "topk": TOPK, "expert_format": "CB3 (3-bit indices, 8-entry bf16 codebook per row)",
+            "shared_format": "int8 per-output-channel, fp32 scales",
+            "l2": "inputs larger than L2: 16 resident layers (1.47 GB each) cycled, ~0.5 GB of fresh weights per step",
+            "parallelism": f"replicas x{n_gpus}" if n_gpus > 1 else "single GPU"}
+
+
+# ------------------------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """NVML polling thread: SM clock and throttle reasons while the timed region runs."""
+
+    def __init__(self, index, period_s=0.002):
+        self.index, self.period = index, period_s
+        self.samples, self.stop_ev, self.th = [], threading.Event(), None
+        self.ok = False
+
+    def __enter__(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv, self.h = nv, nv.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            return self
+
+        def run():
+            nv = self.nv
+            while not self.stop_ev.is_set():
+                try:
+                    self.samples.append((nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM),
+                                         nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)))
+                except Exception:
+                    pass
+                time.sleep(self.period)
+        self.th = threading.Thread(target=run, daemon=True)
+        self.th.start()
+        return self
+
+    def __exit__(self, *a):
+        self.stop_ev.set()
+        if self.th:
+            self.th.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": getattr(self, "max_mhz", None), "reasons": ["unsampled"]}
+        nv = self.nv
+        names = {"sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap, "hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                 "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                 "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                 "hw_power_brake_slowdown": nv.nvmlClocksEventReasonHwPowerBrakeSlowdown}
+        seen = sorted({n for _, r in self.samples for n, b in names.items() if r & b})
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": seen, "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------------------------------------ data
+def make_layer(torch, cbmoe, seed, dev, keep_std=False):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+
+    def cb3(rows, K):
+        words = torch.randint(0, 256, (E * rows * K * 3 // 32 * 4,), dtype=torch.uint8, device=dev, generator=g)
+        cb = (torch.randn((E, rows, 8), device=dev, generator=g) * 0.02).to(torch.bfloat16).float()
+        return words.view(torch.int32).view(E, rows, K * 3 // 32), cb.sort(dim=-1).values.to(torch.bfloat16)
+
+    def q8(n_in, n_out):
+        w = torch.randn((n_in, n_out), device=dev, generator=g) * 0.02
+        s = torch.clamp(w.abs().amax(dim=0, keepdim=True), min=1e-12) / 127.0
+        return torch.clamp(torch.round(w / s), -127, 127).to(torch.int8), s
+
+    gate, up, down = cb3(I, H), cb3(I, H), cb3(H, I)
+    shared = (q8(H, I), q8(H, I), q8(I, H))
+    p = cbmoe.pack_layer(gate, up, down, shared)
+    std = {"gate": gate, "up": up, "down": down, "shared": shared} if keep_std else None
+    return p, std
+
+
+def make_batches(torch, dev, seed, n_batches):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    out = []
+    for _ in range(n_batches):
+        x = torch.randn((N_TOK, H), device=dev, generator=g).to(torch.bfloat16)
+        logits = torch.randn((N_TOK, E), device=dev, generator=g)
+        top, idx = torch.topk(logits, TOPK, dim=-1)
+        w = torch.softmax(top, dim=-1)
+        out.append((x, idx.to(torch.int32).contiguous(), w.contiguous()))
+    return out
+
+
+# ------------------------------------------------------------------------------------------------ CPU legs
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def best_threads(cpu, idx, cb):
+    """Pick the OpenMP thread count that runs one full-size down matvec fastest (the host may be shared)."""
+    import numpy as np
+    x = np.random.default_rng(0).standard_normal((1, idx.shape[-1] * 32 // 3)).astype(np.float32)
+    n = cpu_threads()
+    cands = sorted({1, 2, 4, max(1, n // 2), n})
+    best = (1e9, 1)
+    for t in cands:
+        cpu.cb3_matvec(idx, cb, x, threads=t)
+        t0 = time.perf_counter()
+        for _ in range(3):
+            cpu.cb3_matvec(idx, cb, x, threads=t)
+        best = min(best, ((time.perf_counter() - t0) / 3, t))
+    return best[1]
+
+
+def cpu_layer_sample(std_np, x, idx, w, budget_s, threads):
+    """Run the C oracle token by token on the sample until the budget is spent (at least one token)."""
+    from oracle import cpu
+    n, t_total = 0, 0.0
+    for i in range(x.shape[0]):
+        t0 = time.perf_counter()
+        cpu.moe_layer(x[i:i + 1], idx[i:i + 1], w[i:i + 1], std_np["gate"], std_np["up"], std_np["down"],
+                      std_np["shared"], LIMIT, threads=threads)
+        t_total += time.perf_counter() - t0
+        n += 1
+        if t_total > budget_s:
+            break
+    return n, t_total
+
+
+def std_to_numpy(std):
+    """GPU-generated CB3 tables and int8 leaves -> host NumPy arrays for the C oracle."""
+    import numpy as np
+    import torch
+
+    def tb(t):
+        idx, cb = t
+        return idx.cpu().numpy().view(np.uint32), cb.view(torch.int16).cpu().numpy().view(np.uint16)
+    sh = tuple((q.cpu().numpy(), s.float().cpu().numpy()) for q, s in std["shared"])
+    return {"gate": tb(std["gate"]), "up": tb(std["up"]), "down": tb(std["down"]), "shared": sh}
+
+
+def cpu_layer_tables(seed, experts):
+    """CB3 tables for the reference (CPU) arm, generated on the host: random words for the experts a sample uses
+    (uniform bits = uniform 3-bit indices), zero elsewhere; sorted N(0, 0.02) codebooks; int8 shared expert."""
+    import numpy as np
+    from oracle import cb3, q8
+    rng = np.random.default_rng(seed)
+
+    def table(rows, K):
+        idx = np.zeros((E, rows, K * 3 // 32), np.uint32)
+        for e in experts:
+            idx[e] = rng.integers(0, 2 ** 32, size=idx.shape[1:], dtype=np.uint32)
+        return idx, cb3.make_codebooks(rng, (E, rows)).view(np.uint16)
+
+    def leaf(n_in, n_out):
+        return q8.quantize_array(rng.standard_normal((n_in, n_out)).astype(np.float32) * np.float32(0.02), 1)
+    return {"gate": table(I, H), "up": table(I, H), "down": table(H, I),
+            "shared": (leaf(H, I), leaf(H, I), leaf(I, H))}
+
+
+def run_reference(args):
+    """CPU restatement of the path (the oracle's C port, all host threads) on a bounded sample per step."""
+    import numpy as np
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import cpu, gen
+    cpu.build()
+    rng = np.random.default_rng(1234)
+    n_steps = args.warmup + args.steps
+    xs = gen.activations(rng, n_steps, H).astype(np.float32)
+    idx, w = gen.routing(rng, n_steps, E, TOPK)
+    tabs = cpu_layer_tables(99, sorted(set(idx.reshape(-1).tolist())))
+    threads = best_threads(cpu, tabs["down"][0][idx[0, 0]], tabs["down"][1][idx[0, 0]])
+    times = []
+    for s in range(n_steps):
+        t0 = time.perf_counter()
+        cpu.moe_layer(xs[s:s + 1], idx[s:s + 1], w[s:s + 1], tabs["gate"], tabs["up"], tabs["down"], tabs["shared"],
+                      LIMIT, threads=threads)
+        if s >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = len(times) / total
+    sample = "1 token per step (8 routed experts + shared expert) of the config-1 layer, fp32, C oracle"
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_block(args.gpus),
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "reference path is JAX/Pallas for TPU (JAX absent here): timed arm is the oracle's C port"}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------ our arm
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def load_traffic():
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    import cbmoe
+    from cbmoe._lib import launch_count, profile_enable, profile_read
+
+    layers, std0 = [], None
+    n_layers = max(1, args.layers)
+    for li in range(n_layers):
+        p, std = make_layer(torch, cbmoe, 1000 + li + 100 * rank, dev, keep_std=(li == 0 and rank == 0))
+        layers.append(p)
+        std0 = std0 or std
+    batches = make_batches(torch, dev, 7 + rank, N_BATCHES)
+    fetch = cbmoe.ResidentFetch(path="decode")
+    out = torch.empty((N_TOK, H), dtype=torch.bfloat16, device=dev)
+    torch.cuda.synchronize()
+
+    def step(s):
+        x, idx, w = batches[s % N_BATCHES]
+        fetch.layer(layers[s % n_layers], x, idx, w, LIMIT, out=out)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- value: device-resident inputs, exactly K steps between events
+    for s in range(args.warmup):
+        step(s)
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = launch_count()
+    with ClockSampler(local) as clocks:
+        ev0.record()
+        for s in range(args.steps):
+            step(args.warmup + s)
+        ev1.record()
+        torch.cuda.synchronize()
+    launches = launch_count() - l0
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    barrier()
+    ms_step = ms / args.steps
+    value = world * N_TOK * args.steps / (ms / 1000.0)
+
+    # ---- e2e: pinned host inputs in, bf16 output out, every step, through the public API
+    host = []
+    for x, idx, w in batches[:8]:
+        host.append((x.cpu().pin_memory(), idx.cpu().pin_memory(), w.cpu().pin_memory()))
+    out_h = torch.empty((N_TOK, H), dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty((N_TOK, H), dtype=torch.bfloat16, device=dev)
+    idd = torch.empty((N_TOK, TOPK), dtype=torch.int32, device=dev)
+    wd = torch.empty((N_TOK, TOPK), dtype=torch.float32, device=dev)
+
+    def e2e_step(s):
+        xh, ih, wh = host[s % len(host)]
+        xd.copy_(xh, non_blocking=True)
+        idd.copy_(ih, non_blocking=True)
+        wd.copy_(wh, non_blocking=True)
+        fetch.layer(layers[s % n_layers], xd, idd, wd, LIMIT, out=out)
+        out_h.copy_(out, non_blocking=True)
+
+    for s in range(args.warmup):
+        e2e_step(s)
+    barrier()
+    ev0.record()
+    for s in range(args.steps):
+        e2e_step(args.warmup + s)
+    ev1.record()
+    torch.cuda.synchronize()
+    ms_e2e = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    e2e = world * N_TOK * args.steps / (ms_e2e / 1000.0)
+    h2d = N_TOK * H * 2 + N_TOK * TOPK * 8
+    d2h = N_TOK * H * 2
+
+    # ---- per-kernel event timing over the same K steps (separate pass: events between kernels)
+    profile_read(reset=True)
+    profile_enable(True)
+    for s in range(args.steps):
+        step(args.warmup + s)
+    torch.cuda.synchronize()
+    profile_enable(False)
+    prof = profile_read(reset=True)
+    n_unique = [int(torch.unique(idx).numel()) for _, idx, _ in batches]
+    uniq = [n_unique[(args.warmup + s) % N_BATCHES] for s in range(args.steps)]
+    S = N_TOK * TOPK
+    gateup_bytes = sum(u * (2 * I * H * 3 // 8 + 2 * I * 16) + N_TOK * H * 2 + S * I * 4 for u in uniq)
+    down_bytes = sum(u * (H * I * 3 // 8 + H * 16) + S * I * 4 + S * H * 4 for u in uniq)
+    layer_bytes = sum(u * CB3_EXPERT_BYTES + SHARED_BYTES + 2 * N_TOK * H * 2 for u in uniq)
+    peak, peak_kind = load_peaks()
+    kern = {}
+    for name, nbytes in (("cb3_gateup", gateup_bytes), ("cb3_down", down_bytes)):
+        if name in prof:
+            n, tms = prof[name]
+            kern[name] = {"launches": n, "avg_us": 1000 * tms / n, "gbs": nbytes / (tms / 1000) / 1e9,
+                          "bytes_per_launch": nbytes / n}
+    for name in ("plan", "w8_gateup", "w8_down_combine"):
+        if name in prof:
+            n, tms = prof[name]
+            kern[name] = {"launches": n, "avg_us": 1000 * tms / n}
+    total_ms = sum(v[1] for v in prof.values())
+    for name in kern:
+        kern[name]["share"] = prof[name][1] / total_ms
+    dom = max(("cb3_gateup", "cb3_down"), key=lambda k: prof.get(k, (0, 0))[1])
+    achieved = kern[dom]["gbs"]
+    traffic = load_traffic().get(dom)
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs (copy bandwidth)",
+                "traffic": traffic, "algorithmic_bytes_per_launch": kern[dom]["bytes_per_launch"]}
+    layer_gbs = layer_bytes / (ms_step * args.steps / 1000.0) / 1e9
+
+    # ---- CPU baseline: the C oracle on a bounded sample of the same workload (rank 0 only)
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import cpu
+        cpu.build()
+        std_np = std_to_numpy(std0)
+        x, idx, w = batches[0]
+        threads = best_threads(cpu, std_np["down"][0][int(idx[0, 0])], std_np["down"][1][int(idx[0, 0])])
+        n, secs = cpu_layer_sample(std_np, x.float().cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(),
+                                   args.cpu_seconds, threads)
+        cpu_baseline = {"value": n / secs, "unit": "tok/s", "cores": threads, "kind": "port",
+                        "sample": f"{n} token(s) of batch 0 of layer 0, one at a time (8 routed experts per token + "
+                                  f"shared expert, fp32), C oracle with OpenMP"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": config_block(world), "clocks": clocks.summary(), "gpu_launches": launches,
+                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                        "ms_per_step": ms_e2e / args.steps},
+                "roofline": roofline,
+                "layer": {"gbs": layer_gbs, "frac_of_peak": layer_gbs / peak,
+                          "algorithmic_bytes_per_step": layer_bytes / args.steps,
+                          "distinct_experts_per_step": sum(uniq) / len(uniq)},
+                "kernels": kern, "cpu_baseline": cpu_baseline}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -118,3 +118,18 @@ def test_routing_generators():
     idx_z, _ = gen.routing(np.random.default_rng(1), 64, 160, 8, zipf=1.1)
     counts = np.bincount(idx_z.reshape(-1), minlength=160)
     assert counts.max() >= 32 and (counts == 0).sum() >= 40          # skewed: hot experts and many idle ones
+
+
+# ------------------------------------------------------------------------------------------ C oracle
+def test_c_oracle_matches_numpy_oracle():
+    from oracle import cpu
+    rng = np.random.default_rng(21)
+    E, H, I, N, k = 6, 256, 128, 3, 2
+    L = gen.moe_layer(rng, E, H, I)
+    x = gen.activations(rng, N, H).astype(np.float32)
+    idx, w = gen.routing(rng, N, E, k)
+    got = cpu.moe_layer(x, idx, w, L["gate"], L["up"], L["down"], L["shared"], gen.LIMIT)
+    want = moe.moe_layer(x, idx, w, L["gate"], L["up"], L["down"], L["shared"], gen.LIMIT)
+    assert moe.max_rel_err(got, want) < 1e-5
+    y = cpu.cb3_matvec(L["down"][0][1], L["down"][1][1], x[:, :I] if False else rng.standard_normal((2, I)).astype(np.float32))
+    assert y.shape == (2, H)
