@@ -262,11 +262,17 @@ def load_peaks():
 
 
 def load_traffic():
+    """{kernel kind: DRAM bytes per launch} from profiles/ncu_traffic.txt (ncu captures of the same kernels)."""
+    out = {}
     try:
-        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
-            return json.load(f)
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.txt")) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) >= 2 and not line.startswith("#"):
+                    out[parts[0]] = float(parts[1])
     except Exception:
-        return {}
+        pass
+    return out
 
 
 def run_ours(args):
