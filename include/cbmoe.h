@@ -126,6 +126,19 @@ int cbmoe_experts_apply(const cbmoe_experts* ex, const uint16_t* x, int N, const
                         int k, float limit, int path, float* y, void* workspace, size_t workspace_bytes,
                         cudaStream_t stream);
 
+/* No counterpart in the reference. cbmoe_experts_apply for callers that cannot allocate device memory (an
+ * engine whose allocator owns all device memory and passes only its own buffers, a plugin host that forbids
+ * allocation inside execute, host code that must not block on cudaMalloc). Same inputs and output as
+ * cbmoe_experts_apply on the decode path, but no workspace argument: scratch lives in a fixed device array of
+ * CBMOE_NOALLOC_SCRATCH_BYTES inside the library, held on every GPU that loads the library until exit. Returns
+ * CBMOE_ERR_WORKSPACE when the request needs more scratch than that (e.g. 160 experts, hidden 5120,
+ * intermediate 1536, top-8: up to 64 tokens fit). The first call on a device looks up the array's device address
+ * (make it before any stream capture). All calls on a device share the array: calls that overlap on the GPU race.
+ * Allocates nothing: no cudaMalloc, cudaFree or allocating library call. */
+#define CBMOE_NOALLOC_SCRATCH_BYTES (24u << 20)
+int cbmoe_experts_apply_noalloc(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx,
+                                const float* w, int k, float limit, float* y, cudaStream_t stream);
+
 /* moe_dense below the router (model.py:840-856): routed experts + int8 shared expert (model.py:125-127),
  * out bf16 [N, H]. */
 int cbmoe_moe_layer(const cbmoe_experts* ex, const cbmoe_shared* sh, const uint16_t* x, int N, const int32_t* idx,

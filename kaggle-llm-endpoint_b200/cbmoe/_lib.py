@@ -51,6 +51,8 @@ SIGNATURES = {
     "cbmoe_workspace_bytes": (c_size_t, [ctypes.POINTER(Experts), c_int, c_int, c_int]),
     "cbmoe_experts_apply": (c_int, [ctypes.POINTER(Experts), c_void_p, c_int, c_void_p, c_void_p, c_int, c_float,
                                     c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "cbmoe_experts_apply_noalloc": (c_int, [ctypes.POINTER(Experts), c_void_p, c_int, c_void_p, c_void_p, c_int,
+                                            c_float, c_void_p, c_void_p]),
     "cbmoe_moe_layer": (c_int, [ctypes.POINTER(Experts), ctypes.POINTER(Shared), c_void_p, c_int, c_void_p,
                                 c_void_p, c_int, c_float, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "cbmoe_matvec_workspace_bytes": (c_size_t, [c_int]),

@@ -2,6 +2,7 @@
 // sequence of one call. The drop-in boundary is ResidentFetch.apply (resident.py:100-108) and moe_dense below the
 // router (model.py:840-856).
 #include <cstdio>
+#include <mutex>
 
 #include "decode.cuh"
 
@@ -289,4 +290,57 @@ extern "C" int cbmoe_w8_linear(const void* qk, const float* s, int scale_axis, i
   p.N = N;
   p.y_out = y;
   return decode_w8_single(p, decode_nt(N), stream);
+}
+
+// ------------------------------------------------------------------------------------------------------
+// cbmoe_experts_apply_noalloc: cbmoe_experts_apply for callers that cannot allocate device memory.
+//
+// The other entry points take a caller-provided workspace. Some callers cannot provide one: an inference
+// engine that carves all device memory up front with its own allocator and hands a plugin only the buffers it
+// owns, a plugin host that forbids allocation inside its execute callback, or host code that must not block on
+// cudaMalloc (which can synchronize the device). This entry point keeps its scratch in a file-scope device array
+// instead. The array is part of the library image: every GPU that loads the library holds
+// kNoAllocScratchBytes (24 MiB) of device memory for it until the process exits, whether or not this entry point
+// is ever called. Requests that need more scratch than that are rejected with CBMOE_ERR_WORKSPACE.
+//
+// In host code the name `g_noalloc_scratch` is only a host-side stand-in for the device array, not its device
+// address, so it is never handed to a kernel. The first call on each device, with that device current, looks
+// the address up with cudaGetSymbolAddress (return code checked) and caches it per device; make that first call
+// before any stream capture begins. Every call on a device shares the one array, which keeps whatever the last
+// call left in it: calls that overlap on the GPU (different streams with no ordering between them) race on it.
+// Nothing in the array has to start at zero: the routing-plan kernel writes every plan field before it is read,
+// and the expert kernels write every h / y row before a later kernel reads it.
+namespace {
+constexpr size_t kNoAllocScratchBytes = CBMOE_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {nullptr};
+}  // namespace
+
+extern "C" int cbmoe_experts_apply_noalloc(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx,
+                                           const float* w, int k, float limit, float* y, cudaStream_t stream) {
+  int rc = check_common(ex, x, N, idx, w, k, CBMOE_PATH_DECODE);
+  if (rc) return rc;
+  if (N > 0 && !y) return CBMOE_ERR_INVALID;
+  if (N == 0) return CBMOE_OK;
+  const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k);
+  if (W.total > kNoAllocScratchBytes) return CBMOE_ERR_WORKSPACE;   // request needs more than the fixed array
+  int dev = 0;
+  CBMOE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return CBMOE_ERR_UNSUPPORTED;
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (g_noalloc_addr[dev] == nullptr) {
+      void* p = nullptr;
+      CBMOE_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+      g_noalloc_addr[dev] = p;
+    }
+    scratch = g_noalloc_addr[dev];
+  }
+  uint8_t* ws = static_cast<uint8_t*>(scratch);
+  rc = routed_decode(ex, x, N, idx, w, k, limit, ws, W, stream);
+  if (rc) return rc;
+  const int32_t* plan = reinterpret_cast<const int32_t*>(ws + W.plan);
+  return launch_combine(reinterpret_cast<const float*>(ws + W.y), plan + W.L.off[9], w, N, k, ex->H, y, stream);
 }
