@@ -29,23 +29,45 @@ PlanLayoutHost host_plan_layout(int T, int k, int E, int tm, int pass_tokens) {
 // Tokens per expert pass of the decode kernels for a batch of N tokens (each token picks an expert at most once).
 int decode_nt(int N) { return N <= 8 ? 1 : (N <= 16 ? 2 : 4); }
 
-// Workspace of the decode path: [plan | h (Rp x 2I bf16) | y_sorted (Rp x H f32) | h_shared (N x 2I bf16)].
+// Workspace of the decode path:
+//   plan | h (Rp x 2I bf16) | y_sorted (Rp x H f32) | h_shared (N x 2I bf16) |
+//   scheduling words: routed [gate/up next, down next, gate/up split counters...] (zeroed by the plan kernel),
+//                     shared [gate/up next, down next, split counters...] (zeroed by a memset on the side stream) |
+//   split-K partial sums of the routed gate/up, the shared gate/up and the shared down.
 struct DecodeWorkspace {
-  size_t plan, h, y, hs, total;
-  int nt, Rp;
+  size_t plan, h, y, hs, sched, part_gu, part_sgu, part_sdn, total;
+  int nt, Rp, P, Ps, RB_gu, RB_dn;
+  int kq_gu, kq_sgu, kq_sdn;
+  int n_zero_routed, n_zero_shared;   // words
   PlanLayoutHost L;
 };
 
 DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k) {
   DecodeWorkspace w;
   w.nt = decode_nt(N);
-  w.L = host_plan_layout(N, k, E, 1, 8 * w.nt);
+  const int pt = 8 * w.nt;
+  w.L = host_plan_layout(N, k, E, 1, pt);
   w.Rp = (int)(w.L.off[8] - w.L.off[7]);
+  w.P = (int)(w.L.off[11] - w.L.off[10]);
+  w.Ps = (N + pt - 1) / pt;
+  w.RB_gu = I / kRowsPerBlock;
+  w.RB_dn = H / kRowsPerBlock;
+  const int KS_gu = H / kStageK, KS_dn = I / kStageK;
+  // K splits: small batches have few (expert, row block) items; splitting K evens out the SMs' share of work
+  w.kq_gu = N <= 16 ? (KS_gu < 4 ? KS_gu : 4) : 1;
+  w.kq_sgu = N <= 16 ? (KS_gu < 5 ? KS_gu : 5) : 1;
+  w.kq_sdn = 1;   // measured: the last-arriver reduction costs more than it balances on this 80-block kernel
+  w.n_zero_routed = 2 + w.P * w.RB_gu;
+  w.n_zero_shared = 2 + w.Ps * w.RB_gu + w.Ps * w.RB_dn;
   w.plan = 0;
   w.h = align_up((size_t)w.L.off[13] * 4);
   w.y = w.h + align_up((size_t)w.Rp * 2 * I * 2);
   w.hs = w.y + align_up((size_t)w.Rp * H * 4);
-  w.total = w.hs + align_up((size_t)N * 2 * I * 2);
+  w.sched = w.hs + align_up((size_t)N * 2 * I * 2);
+  w.part_gu = w.sched + align_up((size_t)(w.n_zero_routed + w.n_zero_shared) * 4);
+  w.part_sgu = w.part_gu + (w.kq_gu > 1 ? align_up((size_t)w.kq_gu * w.Rp * 2 * I * 4) : 0);
+  w.part_sdn = w.part_sgu + (w.kq_sgu > 1 ? align_up((size_t)w.kq_sgu * N * 2 * I * 4) : 0);
+  w.total = w.part_sdn + (w.kq_sdn > 1 ? align_up((size_t)w.kq_sdn * N * H * 4) : 0);
   return w;
 }
 
@@ -59,21 +81,47 @@ bool experts_ok(const cbmoe_experts* ex) {
 
 bool shared_ok(const cbmoe_shared* sh) {
   return sh && sh->gateup_q && sh->gate_s && sh->up_s && sh->down_q && sh->down_s &&
-         (sh->scale_axis == 0 || sh->scale_axis == 1) && aligned16(sh->gateup_q) && aligned16(sh->down_q);
+         (sh->scale_axis == 0 || sh->scale_axis == 1) && aligned16(sh->gateup_q) && aligned16(sh->down_q) &&
+         aligned16(sh->gate_s) && aligned16(sh->up_s) && aligned16(sh->down_s);
 }
 
 DecodeParams base_params() {
   DecodeParams p{};
   p.E = 1;
   p.topk = 1;
+  p.KQ = 1;
   return p;
+}
+
+// Per host thread and device: a second stream and two events, so the shared expert's gate/up (independent of
+// the routing) runs concurrently with the routed experts: fork after the caller's prior work, join before the
+// shared down + combine. Created on first use; stream-ordered, so the sequence also records into a graph capture.
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+thread_local SideStream t_side[64];
+
+int side_stream(SideStream** out) {
+  int dev = 0;
+  CBMOE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return CBMOE_ERR_UNSUPPORTED;
+  SideStream& ss = t_side[dev];
+  if (ss.s == nullptr) {
+    CBMOE_CUDA_TRY(cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking));
+    CBMOE_CUDA_TRY(cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming));
+    CBMOE_CUDA_TRY(cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming));
+  }
+  *out = &ss;
+  return CBMOE_OK;
 }
 
 // Plan + routed gate/up + routed down into the workspace; returns the plan pointer through *plan_out.
 int routed_decode(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx, const float* w, int k,
                   float limit, uint8_t* ws, const DecodeWorkspace& W, cudaStream_t stream) {
   int32_t* plan = reinterpret_cast<int32_t*>(ws + W.plan);
-  int rc = launch_route_plan(idx, w, N, k, ex->E, 1, 8 * W.nt, plan, stream);
+  int* sched = reinterpret_cast<int*>(ws + W.sched);
+  int rc = launch_route_plan(idx, w, N, k, ex->E, 1, 8 * W.nt, plan, stream, sched, W.n_zero_routed);
   if (rc) return rc;
   uint16_t* h = reinterpret_cast<uint16_t*>(ws + W.h);
   float* ys = reinterpret_cast<float*>(ws + W.y);
@@ -96,6 +144,11 @@ int routed_decode(const cbmoe_experts* ex, const uint16_t* x, int N, const int32
   p.E = ex->E;
   p.limit = limit;
   p.h_out = h;
+  p.KQ = W.kq_gu;
+  p.sched = sched;
+  p.done = sched + 2;
+  p.part = reinterpret_cast<float*>(ws + W.part_gu);
+  p.part_rows = W.Rp;
   rc = decode_cb3_gateup(p, W.nt, stream);
   if (rc) return rc;
 
@@ -111,6 +164,10 @@ int routed_decode(const cbmoe_experts* ex, const uint16_t* x, int N, const int32
   d.tok_row = nullptr;
   d.h_out = nullptr;
   d.y_out = ys;
+  d.KQ = 1;
+  d.sched = sched + 1;
+  d.done = nullptr;
+  d.part = nullptr;
   return decode_cb3_down(d, W.nt, stream);
 }
 
@@ -207,10 +264,14 @@ extern "C" int cbmoe_moe_layer(const cbmoe_experts* ex, const cbmoe_shared* sh, 
   const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k);
   if (!workspace || workspace_bytes < W.total) return CBMOE_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  rc = routed_decode(ex, x, N, idx, w, k, limit, ws, W, stream);
-  if (rc) return rc;
-  const int32_t* plan = reinterpret_cast<const int32_t*>(ws + W.plan);
   uint16_t* hs = reinterpret_cast<uint16_t*>(ws + W.hs);
+  SideStream* side = nullptr;
+  rc = side_stream(&side);
+  if (rc) return rc;
+  CBMOE_CUDA_TRY(cudaEventRecord(side->fork, stream));
+  CBMOE_CUDA_TRY(cudaStreamWaitEvent(side->s, side->fork, 0));
+  int* sched_sh = reinterpret_cast<int*>(ws + W.sched) + W.n_zero_routed;
+  CBMOE_CUDA_TRY(cudaMemsetAsync(sched_sh, 0, (size_t)W.n_zero_shared * 4, side->s));
 
   DecodeParams p = base_params();
   p.wq = static_cast<const uint8_t*>(sh->gateup_q);
@@ -225,8 +286,19 @@ extern "C" int cbmoe_moe_layer(const cbmoe_experts* ex, const cbmoe_shared* sh, 
   p.N = N;
   p.limit = limit;
   p.h_out = hs;
-  rc = decode_w8_gateup(p, decode_nt(N), stream);
+  p.KQ = W.kq_sgu;
+  p.sched = sched_sh;
+  p.done = sched_sh + 2;
+  p.part = reinterpret_cast<float*>(ws + W.part_sgu);
+  p.part_rows = N;
+  rc = decode_w8_gateup(p, decode_nt(N), side->s);
   if (rc) return rc;
+  CBMOE_CUDA_TRY(cudaEventRecord(side->join, side->s));
+
+  rc = routed_decode(ex, x, N, idx, w, k, limit, ws, W, stream);
+  CBMOE_CUDA_TRY(cudaStreamWaitEvent(stream, side->join, 0));   // join even when a routed launch failed
+  if (rc) return rc;
+  const int32_t* plan = reinterpret_cast<const int32_t*>(ws + W.plan);
 
   DecodeParams d = base_params();
   d.wq = static_cast<const uint8_t*>(sh->down_q);
@@ -244,6 +316,11 @@ extern "C" int cbmoe_moe_layer(const cbmoe_experts* ex, const cbmoe_shared* sh, 
   d.wts = w;
   d.topk = k;
   d.out_bf16 = out;
+  d.KQ = W.kq_sdn;
+  d.sched = sched_sh + 1;
+  d.done = sched_sh + 2 + W.Ps * W.RB_gu;
+  d.part = reinterpret_cast<float*>(ws + W.part_sdn);
+  d.part_rows = N;
   return decode_w8_down_combine(d, decode_nt(N), stream);
 }
 
@@ -274,7 +351,7 @@ extern "C" int cbmoe_w8_linear(const void* qk, const float* s, int scale_axis, i
   (void)workspace;
   (void)workspace_bytes;
   if (!qk || !s || rows <= 0 || K <= 0 || rows % kRowsPerBlock || K % kStageK || N < 0 ||
-      (scale_axis != 0 && scale_axis != 1))
+      (scale_axis != 0 && scale_axis != 1) || !aligned16(s))
     return CBMOE_ERR_INVALID;
   if (N > 0 && (!x || !y || !aligned16(x) || !aligned16(qk))) return CBMOE_ERR_INVALID;
   if (N == 0) return CBMOE_OK;

@@ -5,7 +5,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
-#include "../../include/cbmoe.h"
+#include "cbmoe.h"
 
 namespace cbmoe {
 
@@ -62,6 +62,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
     if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicOr(&g_device_errors, CBMOE_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
+// The same wait for a warp that is usually early (a producer waiting for consumers to free a stage): it sleeps
+// between polls, so its spinning does not take issue slots from the consumer warps of the same scheduler.
+__device__ __forceinline__ bool mbar_wait_sleepy(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  uint32_t ns = 64;
+  while (!mbar_try_wait(bar, parity)) {
+    __nanosleep(ns);
+    if (ns < 1024) ns <<= 1;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
       atomicOr(&g_device_errors, CBMOE_DEVERR_TIMEOUT);
       return false;
     }

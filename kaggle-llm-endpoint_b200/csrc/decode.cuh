@@ -34,6 +34,12 @@ struct DecodeParams {
   const float* wts;         //          routing weights [N, topk]
   int topk;
   uint16_t* out_bf16;       //          [N][rows]
+  // work distribution
+  int KQ;                   // K splits per (pass, row block): 1, or > 1 with partial sums + last-arriver epilogue
+  int* sched;               // [0] = next-item counter, zero at launch (nullptr: static round-robin over items)
+  int* done;                // KQ > 1: arrival counter per (pass, row block), zero at launch, reset by the last
+  float* part;              // KQ > 1: partial sums [KQ][part_rows][NMAT][rows]
+  int part_rows;
 };
 
 int decode_cb3_gateup(const DecodeParams& p, int nt, cudaStream_t s);
@@ -45,6 +51,6 @@ int decode_w8_single(const DecodeParams& p, int nt, cudaStream_t s);
 int launch_combine(const float* y_sorted, const int* row_slot, const float* wts, int N, int topk, int H, float* y,
                    cudaStream_t stream);
 int launch_route_plan(const int32_t* idx, const float* w, int T, int k, int E, int tm, int pass_tokens,
-                      int32_t* plan, cudaStream_t stream);
+                      int32_t* plan, cudaStream_t stream, int* zero = nullptr, int n_zero = 0);
 
 }  // namespace cbmoe

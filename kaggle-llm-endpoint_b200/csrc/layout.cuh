@@ -54,6 +54,10 @@ struct Codebook {
 };
 
 // One chunk of one matrix: 3 index words of this lane -> fragments a[s][0..3] for the 4 MMA steps.
+//   selectors of row g:   w0 & 0x7.. (s = 0 low half, s = 1 high half), w1 & 0x7.. (s = 2, 3)
+//   selectors of row g+8: w2 & 0x7.. (s = 0, 1); s = 2, 3 from the spare bits: (w0 & 0x8..) >> 3 |
+//                         (w1 & 0x8..) >> 2 | (w2 & 0x8..) >> 1.
+// (Moving the shifts to integer multiply-adds on the FMA pipe was measured slower: longer dependency latency.)
 __device__ __forceinline__ void cb3k_dequant_chunk(uint32_t w0, uint32_t w1, uint32_t w2, const Codebook& cg,
                                                    const Codebook& ch, uint32_t (&a)[4][4]) {
   const uint32_t g01 = w0 & 0x77777777u;
@@ -75,32 +79,40 @@ __device__ __forceinline__ void cb3k_dequant_chunk(uint32_t w0, uint32_t w1, uin
   }
 }
 
-// int8 pair (bytes b, b+1 of word q) of a row with scale(s) -> bf16x2 of bf16(f32(q) * s) (quant8.py:94).
-__device__ __forceinline__ uint32_t w8_pair(uint32_t q, int b, float s0, float s1) {
-  const float v0 = static_cast<float>(static_cast<int8_t>((q >> (8 * b)) & 0xFFu)) * s0;
-  const float v1 = static_cast<float>(static_cast<int8_t>((q >> (8 * b + 8)) & 0xFFu)) * s1;
-  return pack_bf16x2(v0, v1);
+// 4 signed bytes of q -> exact floats, without the conversion unit: byte ^ 0x80 placed in the mantissa of 2^23
+// gives 2^23 + 128 + b, and one subtraction of 2^23 + 128 leaves b.
+__device__ __forceinline__ void w8_bytes_to_f32(uint32_t q, float (&f)[4]) {
+  const uint32_t qx = q ^ 0x80808080u;
+  constexpr float kBias = 8388736.0f;  // 2^23 + 128
+  f[0] = __uint_as_float(prmt(qx, 0x4B000000u, 0x7540u)) - kBias;
+  f[1] = __uint_as_float(prmt(qx, 0x4B000000u, 0x7541u)) - kBias;
+  f[2] = __uint_as_float(prmt(qx, 0x4B000000u, 0x7542u)) - kBias;
+  f[3] = __uint_as_float(prmt(qx, 0x4B000000u, 0x7543u)) - kBias;
 }
 
-// One chunk of one W8K matrix: qg/qh = this lane's 16 int8 of rows g and g+8 (4 words each). Scales: per row
-// (sg, sh) when kg == nullptr, else per input from kg[0..15] (this lane's 16 inputs of the chunk).
+// One chunk of one W8K matrix: qg/qh = this lane's 16 int8 of rows g and g+8 (4 words each) -> bf16 fragments
+// of bf16(f32(q) * s) (quant8.py:94). Scales: per row (sg, sh) when kscale == nullptr, else per input from
+// kscale[0..15] (this lane's 16 inputs of the chunk).
 __device__ __forceinline__ void w8k_dequant_chunk(const uint4& qg, const uint4& qh, float sg, float sh,
                                                   const float* kscale, uint32_t (&a)[4][4]) {
   const uint32_t g[4] = {qg.x, qg.y, qg.z, qg.w};
   const uint32_t h[4] = {qh.x, qh.y, qh.z, qh.w};
 #pragma unroll
   for (int s = 0; s < 4; ++s) {
+    float fg[4], fh[4];
+    w8_bytes_to_f32(g[s], fg);
+    w8_bytes_to_f32(h[s], fh);
     if (kscale == nullptr) {
-      a[s][0] = w8_pair(g[s], 0, sg, sg);
-      a[s][2] = w8_pair(g[s], 2, sg, sg);
-      a[s][1] = w8_pair(h[s], 0, sh, sh);
-      a[s][3] = w8_pair(h[s], 2, sh, sh);
+      a[s][0] = pack_bf16x2(fg[0] * sg, fg[1] * sg);
+      a[s][2] = pack_bf16x2(fg[2] * sg, fg[3] * sg);
+      a[s][1] = pack_bf16x2(fh[0] * sh, fh[1] * sh);
+      a[s][3] = pack_bf16x2(fh[2] * sh, fh[3] * sh);
     } else {
       const float k0 = kscale[4 * s], k1 = kscale[4 * s + 1], k2 = kscale[4 * s + 2], k3 = kscale[4 * s + 3];
-      a[s][0] = w8_pair(g[s], 0, k0, k1);
-      a[s][2] = w8_pair(g[s], 2, k2, k3);
-      a[s][1] = w8_pair(h[s], 0, k0, k1);
-      a[s][3] = w8_pair(h[s], 2, k2, k3);
+      a[s][0] = pack_bf16x2(fg[0] * k0, fg[1] * k1);
+      a[s][2] = pack_bf16x2(fg[2] * k2, fg[3] * k3);
+      a[s][1] = pack_bf16x2(fh[0] * k0, fh[1] * k1);
+      a[s][3] = pack_bf16x2(fh[2] * k2, fh[3] * k3);
     }
   }
 }

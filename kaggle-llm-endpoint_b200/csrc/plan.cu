@@ -59,12 +59,13 @@ __device__ __forceinline__ int warp_exclusive_scan(int v, int* total) {
 __global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(const int32_t* __restrict__ idx,
                                                                   const float* __restrict__ wts, int T, int k, int E,
                                                                   int tm, int pass_tokens, int32_t* __restrict__ plan,
-                                                                  PlanLayout L) {
+                                                                  PlanLayout L, int* __restrict__ zero, int n_zero) {
   extern __shared__ int sm[];
   int* cnt = sm;                               // [kPlanWarps][E]
   int* counts = cnt + kPlanWarps * E;          // [E]
   int* ends = counts + E;                      // [E] block end (exclusive) per expert
   __shared__ int s_tot[4];
+  __shared__ int s_chunk[4][32];
 
   const int S = T * k;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -73,6 +74,7 @@ __global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(const int32_t*
   const int end = min(S, beg + per_warp);
 
   for (int i = threadIdx.x; i < kPlanWarps * E; i += kPlanThreads) cnt[i] = 0;
+  for (int i = threadIdx.x; i < n_zero; i += kPlanThreads) zero[i] = 0;   // scheduling words of the next kernels
   __syncthreads();
 
   // pass A: per-warp per-expert counts
@@ -96,6 +98,7 @@ __global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(const int32_t*
   int32_t* pass_cnt = plan + L.off[12];
   const int P = (int)(L.off[11] - L.off[10]);
 
+  // per-expert totals
   for (int e = threadIdx.x; e < E; e += kPlanThreads) {
     int c = 0;
     for (int w = 0; w < kPlanWarps; ++w) c += cnt[w * E + e];
@@ -103,52 +106,71 @@ __global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(const int32_t*
   }
   __syncthreads();
 
-  // scans over experts (warp 0), 32 experts per step
-  if (warp == 0) {
-    int run_rows = 0, run_blocks = 0, run_pass = 0, run_act = 0;
-    for (int e0 = 0; e0 < E; e0 += 32) {
-      const int e = e0 + lane;
-      const int c = (e < E) ? counts[e] : 0;
-      const int nb = (c + tm - 1) / tm;
-      const int np = (c + pass_tokens - 1) / pass_tokens;
-      int t_rows, t_blocks, t_pass, t_act;
-      const int x_rows = warp_exclusive_scan(nb * tm, &t_rows);
-      const int x_blocks = warp_exclusive_scan(nb, &t_blocks);
-      const int x_pass = warp_exclusive_scan(np, &t_pass);
-      const int x_act = warp_exclusive_scan(c > 0 ? 1 : 0, &t_act);
-      if (e < E) {
-        const int rs = run_rows + x_rows;
-        counts_g[e] = c;
-        row_start[e] = rs;
-        ends[e] = run_blocks + x_blocks + nb;
-        if (c > 0) act[run_act + x_act] = e;
-        for (int p = 0; p < np; ++p) {
-          const int q = run_pass + x_pass + p;
-          pass_expert[q] = e;
-          pass_row0[q] = rs + p * pass_tokens;
-          pass_cnt[q] = min(pass_tokens, c - p * pass_tokens);
-        }
-        // turn this expert's per-warp counts into per-warp starting rows
-        int run = rs;
-        for (int w = 0; w < kPlanWarps; ++w) {
-          const int v = cnt[w * E + e];
-          cnt[w * E + e] = run;
-          run += v;
-        }
-      }
-      run_rows += t_rows;
-      run_blocks += t_blocks;
-      run_pass += t_pass;
-      run_act += t_act;
-    }
+  // scans over experts, 32 experts per chunk, chunks spread over the warps: (1) per-chunk totals
+  const int n_chunks = (E + 31) / 32;
+  for (int q = warp; q < n_chunks; q += kPlanWarps) {
+    const int e = q * 32 + lane;
+    const int c = (e < E) ? counts[e] : 0;
+    const int nb = (c + tm - 1) / tm;
+    const int np = (c + pass_tokens - 1) / pass_tokens;
+    int t_rows, t_blocks, t_pass, t_act;
+    warp_exclusive_scan(nb * tm, &t_rows);
+    warp_exclusive_scan(nb, &t_blocks);
+    warp_exclusive_scan(np, &t_pass);
+    warp_exclusive_scan(c > 0 ? 1 : 0, &t_act);
     if (lane == 0) {
-      s_tot[0] = run_act;
-      s_tot[1] = run_blocks;
-      s_tot[2] = run_pass;
-      plan[L.off[3]] = run_act;
-      plan[L.off[4]] = run_blocks;
-      plan[L.off[5]] = run_pass;
+      s_chunk[0][q] = t_rows;
+      s_chunk[1][q] = t_blocks;
+      s_chunk[2][q] = t_pass;
+      s_chunk[3][q] = t_act;
     }
+  }
+  __syncthreads();
+  // (2) every warp scans the chunk totals itself, then finishes its own chunks
+  int c_rows, c_blocks, c_pass, c_act, tot_rows, tot_blocks, tot_pass, tot_act;
+  {
+    const bool in = lane < n_chunks;
+    c_rows = warp_exclusive_scan(in ? s_chunk[0][lane] : 0, &tot_rows);
+    c_blocks = warp_exclusive_scan(in ? s_chunk[1][lane] : 0, &tot_blocks);
+    c_pass = warp_exclusive_scan(in ? s_chunk[2][lane] : 0, &tot_pass);
+    c_act = warp_exclusive_scan(in ? s_chunk[3][lane] : 0, &tot_act);
+  }
+  for (int q = warp; q < n_chunks; q += kPlanWarps) {
+    const int e = q * 32 + lane;
+    const int c = (e < E) ? counts[e] : 0;
+    const int nb = (c + tm - 1) / tm;
+    const int np = (c + pass_tokens - 1) / pass_tokens;
+    int dummy;
+    const int x_rows = warp_exclusive_scan(nb * tm, &dummy) + __shfl_sync(0xffffffffu, c_rows, q);
+    const int x_blocks = warp_exclusive_scan(nb, &dummy) + __shfl_sync(0xffffffffu, c_blocks, q);
+    const int x_pass = warp_exclusive_scan(np, &dummy) + __shfl_sync(0xffffffffu, c_pass, q);
+    const int x_act = warp_exclusive_scan(c > 0 ? 1 : 0, &dummy) + __shfl_sync(0xffffffffu, c_act, q);
+    if (e < E) {
+      counts_g[e] = c;
+      row_start[e] = x_rows;
+      ends[e] = x_blocks + nb;
+      if (c > 0) act[x_act] = e;
+      for (int p = 0; p < np; ++p) {
+        pass_expert[x_pass + p] = e;
+        pass_row0[x_pass + p] = x_rows + p * pass_tokens;
+        pass_cnt[x_pass + p] = min(pass_tokens, c - p * pass_tokens);
+      }
+      // this expert's per-warp counts -> per-warp starting rows
+      int run = x_rows;
+      for (int w = 0; w < kPlanWarps; ++w) {
+        const int v = cnt[w * E + e];
+        cnt[w * E + e] = run;
+        run += v;
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    s_tot[0] = tot_act;
+    s_tot[1] = tot_blocks;
+    s_tot[2] = tot_pass;
+    plan[L.off[3]] = tot_act;
+    plan[L.off[4]] = tot_blocks;
+    plan[L.off[5]] = tot_pass;
   }
   // padding rows and unused list entries
   const int Rp = (int)(L.off[8] - L.off[7]);
@@ -207,7 +229,7 @@ __global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(const int32_t*
 size_t plan_smem_bytes(int E) { return (size_t)(kPlanWarps + 2) * E * sizeof(int); }
 
 int launch_route_plan(const int32_t* idx, const float* w, int T, int k, int E, int tm, int pass_tokens,
-                      int32_t* plan, cudaStream_t stream) {
+                      int32_t* plan, cudaStream_t stream, int* zero, int n_zero) {
   const PlanLayout L = plan_layout(T, k, E, tm, pass_tokens);
   const size_t smem = plan_smem_bytes(E);
   static bool attr_set = false;
@@ -217,7 +239,7 @@ int launch_route_plan(const int32_t* idx, const float* w, int T, int k, int E, i
     attr_set = true;
   }
   prof_begin(kProfPlan, stream);
-  route_plan_kernel<<<1, kPlanThreads, smem, stream>>>(idx, w, T, k, E, tm, pass_tokens, plan, L);
+  route_plan_kernel<<<1, kPlanThreads, smem, stream>>>(idx, w, T, k, E, tm, pass_tokens, plan, L, zero, n_zero);
   prof_end(kProfPlan, stream);
   CBMOE_CUDA_TRY(cudaGetLastError());
   return CBMOE_OK;
@@ -240,5 +262,5 @@ extern "C" int cbmoe_route_plan(const int32_t* idx, const float* w, int T, int k
     return CBMOE_ERR_INVALID;
   const cbmoe::PlanLayout L = cbmoe::plan_layout(T, k, E, tm, pass_tokens);
   if (plan_bytes < (size_t)L.off[13] * 4) return CBMOE_ERR_WORKSPACE;
-  return cbmoe::launch_route_plan(idx, w, T, k, E, tm, pass_tokens, static_cast<int32_t*>(plan), stream);
+  return cbmoe::launch_route_plan(idx, w, T, k, E, tm, pass_tokens, static_cast<int32_t*>(plan), stream, nullptr, 0);
 }

@@ -2,7 +2,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
-#include "../../include/cbmoe.h"
+#include "cbmoe.h"
 
 namespace cbmoe {
 
