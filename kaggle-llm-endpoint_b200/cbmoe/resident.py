@@ -57,7 +57,7 @@ class ResidentFetch:
     `gather_max_rows` (slots N*k at or below which the decode kernels run; above it the grouped path), and
     `path` to force "decode" or "grouped"."""
 
-    def __init__(self, qtypes=None, D=None, ml=None, out_dtype=torch.float32, gather_max_rows=4096, path="auto"):
+    def __init__(self, qtypes=None, D=None, ml=None, out_dtype=torch.float32, gather_max_rows=1024, path="auto"):
         self.qtypes = qtypes or {}
         self.D, self.ml = D, ml
         self.out_dtype = out_dtype

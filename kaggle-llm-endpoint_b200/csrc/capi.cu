@@ -5,6 +5,7 @@
 #include <mutex>
 
 #include "decode.cuh"
+#include "grouped.cuh"
 
 namespace cbmoe {
 
@@ -171,6 +172,72 @@ int routed_decode(const cbmoe_experts* ex, const uint16_t* x, int N, const int32
   return decode_cb3_down(d, W.nt, stream);
 }
 
+// Slots (N*k) above which CBMOE_PATH_AUTO takes the grouped tensor-core path.
+constexpr int kGroupedMinSlots = 1024;
+// Token rows above which cbmoe_w8_linear runs the tcgen05 GEMM instead of the decode kernel.
+constexpr int kW8DecodeMaxTokens = 64;
+
+int pick_path(int N, int k, int path) {
+  if (path != CBMOE_PATH_AUTO) return path;
+  return (long long)N * k > kGroupedMinSlots ? CBMOE_PATH_GROUPED : CBMOE_PATH_DECODE;
+}
+
+// Workspace of the grouped path: plan | xs (Rp x H bf16, tokens gathered in expert order) | h (Rp x I bf16) |
+// y_sorted (Rp x H bf16) | shared h (N x I bf16) | shared down (N x H bf16).
+struct GroupedWorkspace {
+  size_t plan, xs, h, y, hs, sy, total;
+  int Rp;
+  PlanLayoutHost L;
+};
+
+GroupedWorkspace grouped_workspace(int E, int H, int I, int N, int k) {
+  GroupedWorkspace w;
+  w.L = host_plan_layout(N, k, E, 1, kGrpTileN);
+  w.Rp = (int)(w.L.off[8] - w.L.off[7]);
+  w.plan = 0;
+  w.xs = align_up((size_t)w.L.off[13] * 4);
+  w.h = w.xs + align_up((size_t)w.Rp * H * 2);
+  w.y = w.h + align_up((size_t)w.Rp * I * 2);
+  w.hs = w.y + align_up((size_t)w.Rp * H * 2);
+  w.sy = w.hs + align_up((size_t)N * I * 2);
+  w.total = w.sy + align_up((size_t)N * H * 2);
+  return w;
+}
+
+// Plan + gather + grouped gate/up + grouped down into the workspace (y_sorted bf16, rows in expert order).
+int routed_grouped(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx, const float* w, int k,
+                   float limit, uint8_t* ws, const GroupedWorkspace& W, cudaStream_t stream) {
+  int32_t* plan = reinterpret_cast<int32_t*>(ws + W.plan);
+  int rc = launch_route_plan(idx, w, N, k, ex->E, 1, kGrpTileN, plan, stream);
+  if (rc) return rc;
+  uint16_t* xs = reinterpret_cast<uint16_t*>(ws + W.xs);
+  uint16_t* h = reinterpret_cast<uint16_t*>(ws + W.h);
+  uint16_t* ys = reinterpret_cast<uint16_t*>(ws + W.y);
+  rc = launch_gather_rows(x, ex->H, plan + W.L.off[7], W.Rp, xs, stream);
+  if (rc) return rc;
+  GroupedParams p{};
+  p.wq = static_cast<const uint8_t*>(ex->gateup_idx);
+  p.cb = static_cast<const uint32_t*>(ex->gateup_cb);
+  p.rows = ex->I;
+  p.K = ex->H;
+  p.pass_expert = plan + W.L.off[10];
+  p.pass_row0 = plan + W.L.off[11];
+  p.pass_cnt = plan + W.L.off[12];
+  p.n_pass = plan + W.L.off[5];
+  p.E = ex->E;
+  p.limit = limit;
+  p.out = h;
+  rc = grouped_cb3_gateup(p, xs, W.Rp, stream);
+  if (rc) return rc;
+  GroupedParams d = p;
+  d.wq = static_cast<const uint8_t*>(ex->down_idx);
+  d.cb = static_cast<const uint32_t*>(ex->down_cb);
+  d.rows = ex->H;
+  d.K = ex->I;
+  d.out = ys;
+  return grouped_cb3_down(d, h, W.Rp, stream);
+}
+
 }  // namespace
 
 void set_last_cuda_error(cudaError_t e) { t_last_cuda_error = (int)e; }
@@ -225,7 +292,7 @@ extern "C" int cbmoe_device_errors(int clear, int* out_host) {
 
 extern "C" size_t cbmoe_workspace_bytes(const cbmoe_experts* ex, int N, int k, int path) {
   if (!ex || N < 0 || k <= 0 || ex->E <= 0) return 0;
-  (void)path;
+  if (pick_path(N, k, path) == CBMOE_PATH_GROUPED) return grouped_workspace(ex->E, ex->H, ex->I, N, k).total;
   return decode_workspace(ex->E, ex->H, ex->I, N, k).total;
 }
 
@@ -234,7 +301,8 @@ static int check_common(const cbmoe_experts* ex, const uint16_t* x, int N, const
   if (!experts_ok(ex) || N < 0 || k <= 0 || k > 64) return CBMOE_ERR_INVALID;
   if (N > 0 && (!x || !idx || !w || !aligned16(x))) return CBMOE_ERR_INVALID;
   if (path != CBMOE_PATH_AUTO && path != CBMOE_PATH_DECODE && path != CBMOE_PATH_GROUPED) return CBMOE_ERR_INVALID;
-  if (path == CBMOE_PATH_GROUPED) return CBMOE_ERR_UNSUPPORTED;
+  if (pick_path(N, k, path) == CBMOE_PATH_GROUPED && (ex->I % kGrpTileM || ex->H % kGrpTileM || N > (1 << 24)))
+    return CBMOE_ERR_UNSUPPORTED;
   return CBMOE_OK;
 }
 
@@ -245,6 +313,16 @@ extern "C" int cbmoe_experts_apply(const cbmoe_experts* ex, const uint16_t* x, i
   if (rc) return rc;
   if (N > 0 && !y) return CBMOE_ERR_INVALID;
   if (N == 0) return CBMOE_OK;
+  if (pick_path(N, k, path) == CBMOE_PATH_GROUPED) {
+    const GroupedWorkspace G = grouped_workspace(ex->E, ex->H, ex->I, N, k);
+    if (!workspace || workspace_bytes < G.total) return CBMOE_ERR_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    rc = routed_grouped(ex, x, N, idx, w, k, limit, ws, G, stream);
+    if (rc) return rc;
+    const int32_t* plan = reinterpret_cast<const int32_t*>(ws + G.plan);
+    return launch_combine_bf16(reinterpret_cast<const uint16_t*>(ws + G.y), plan + G.L.off[9], w, N, k, ex->H,
+                               nullptr, y, nullptr, stream);
+  }
   const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k);
   if (!workspace || workspace_bytes < W.total) return CBMOE_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -261,6 +339,40 @@ extern "C" int cbmoe_moe_layer(const cbmoe_experts* ex, const cbmoe_shared* sh, 
   if (rc) return rc;
   if (!shared_ok(sh) || (N > 0 && !out)) return CBMOE_ERR_INVALID;
   if (N == 0) return CBMOE_OK;
+  if (pick_path(N, k, path) == CBMOE_PATH_GROUPED) {
+    const GroupedWorkspace G = grouped_workspace(ex->E, ex->H, ex->I, N, k);
+    if (!workspace || workspace_bytes < G.total) return CBMOE_ERR_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    rc = routed_grouped(ex, x, N, idx, w, k, limit, ws, G, stream);
+    if (rc) return rc;
+    uint16_t* hs = reinterpret_cast<uint16_t*>(ws + G.hs);
+    uint16_t* sy = reinterpret_cast<uint16_t*>(ws + G.sy);
+    GroupedParams p{};
+    p.wq = static_cast<const uint8_t*>(sh->gateup_q);
+    p.s0 = sh->gate_s;
+    p.s1 = sh->up_s;
+    p.scale_axis = sh->scale_axis;
+    p.rows = ex->I;
+    p.K = ex->H;
+    p.N = N;
+    p.E = 1;
+    p.limit = limit;
+    p.out = hs;
+    rc = grouped_w8_gateup(p, x, N, stream);
+    if (rc) return rc;
+    GroupedParams d = p;
+    d.wq = static_cast<const uint8_t*>(sh->down_q);
+    d.s0 = sh->down_s;
+    d.s1 = nullptr;
+    d.rows = ex->H;
+    d.K = ex->I;
+    d.out = sy;
+    rc = grouped_w8_store(d, hs, N, stream);
+    if (rc) return rc;
+    const int32_t* plan = reinterpret_cast<const int32_t*>(ws + G.plan);
+    return launch_combine_bf16(reinterpret_cast<const uint16_t*>(ws + G.y), plan + G.L.off[9], w, N, k, ex->H, sy,
+                               nullptr, out, stream);
+  }
   const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k);
   if (!workspace || workspace_bytes < W.total) return CBMOE_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -355,6 +467,18 @@ extern "C" int cbmoe_w8_linear(const void* qk, const float* s, int scale_axis, i
     return CBMOE_ERR_INVALID;
   if (N > 0 && (!x || !y || !aligned16(x) || !aligned16(qk))) return CBMOE_ERR_INVALID;
   if (N == 0) return CBMOE_OK;
+  if (N > kW8DecodeMaxTokens && rows % kGrpTileM == 0) {
+    GroupedParams g{};
+    g.wq = static_cast<const uint8_t*>(qk);
+    g.s0 = s;
+    g.scale_axis = scale_axis;
+    g.rows = rows;
+    g.K = K;
+    g.N = N;
+    g.E = 1;
+    g.out_f32 = y;
+    return grouped_w8_store_f32(g, x, N, stream);
+  }
   DecodeParams p = base_params();
   p.wq = static_cast<const uint8_t*>(qk);
   p.s0 = s;

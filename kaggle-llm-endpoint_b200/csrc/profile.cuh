@@ -15,7 +15,11 @@ enum ProfKind {
   kProfW8DownCombine = 5, // decode_kernel_t<W8, 1 matrix, COMBINE>
   kProfW8Single = 6,      // decode_kernel_t<W8, 1 matrix, STORE>
   kProfCombine = 7,       // combine_kernel
-  kProfOther = 8,         // layout repacks and dequant checks
+  kProfOther = 8,         // layout repacks, dequant checks, row gathers
+  kProfGrpCb3GateUp = 9,  // grouped_kernel<CB3, gate+up, SWIGLU> (tcgen05)
+  kProfGrpCb3Down = 10,   // grouped_kernel<CB3, down, STORE>
+  kProfGrpW8GateUp = 11,  // grouped_kernel<W8, gate+up, SWIGLU>
+  kProfGrpW8Store = 12,   // grouped_kernel<W8, one matrix, STORE>
   kProfKinds = 16
 };
 
