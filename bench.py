@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="resident layers cycled by the steps (profiling "
                     "captures use 1 to keep device memory small)")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+                    help="decode = config 1 (the default bench line); prefill = config 3 (4096 tokens, tcgen05 path)")
     return ap.parse_args()
 
 
@@ -436,8 +438,107 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------------------------------------ config 3
+T_PREFILL, QKV_OUT = 4096, 96 * 128
+
+
+def load_peaks_tc():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d["bf16_tflops_sustained"]), "measured"
+    except Exception:
+        return 1590.0, 1400.0, "fallback"
+
+
+def run_prefill(args):
+    """Config 3: MoE layer (routed CB3 experts on the grouped tcgen05 path + int8 shared expert) plus the int8 QKV
+    [5120 -> 12288] and O [12288 -> 5120] projections, 4096 tokens, uniform top-8 routing. A step = the layer + QKV
+    + O on one 4096-token batch; two resident layers alternate (weights 1.6 GB per step > L2)."""
+    import torch
+    import cbmoe
+    from cbmoe._lib import launch_count, profile_enable, profile_read
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    n_layers = max(1, min(args.layers, 2))
+    layers = [make_layer(torch, cbmoe, 2000 + i, dev)[0] for i in range(n_layers)]
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+
+    def q8(n_in, n_out):
+        w = torch.randn((n_in, n_out), device=dev, generator=g) * 0.02
+        sc = torch.clamp(w.abs().amax(dim=0, keepdim=True), min=1e-12) / 127.0
+        return cbmoe.ops.pack_w8(torch.clamp(torch.round(w / sc), -127, 127).to(torch.int8)), sc.reshape(-1).contiguous()
+    projs = [(q8(H, QKV_OUT), q8(QKV_OUT, H)) for _ in range(n_layers)]
+    x = torch.randn((T_PREFILL, H), device=dev, generator=g).to(torch.bfloat16)
+    logits = torch.randn((T_PREFILL, E), device=dev, generator=g)
+    top, idx = torch.topk(logits, TOPK, dim=-1)
+    w = torch.softmax(top, dim=-1).contiguous()
+    idx = idx.to(torch.int32).contiguous()
+    fetch = cbmoe.ResidentFetch(path="grouped")
+    out = torch.empty((T_PREFILL, H), dtype=torch.bfloat16, device=dev)
+    att = torch.empty((T_PREFILL, H), dtype=torch.bfloat16, device=dev)
+
+    def step(s):
+        li = s % n_layers
+        (qkv_q, qkv_s), (o_q, o_s) = projs[li]
+        qkv = cbmoe.ops.w8_linear(qkv_q, qkv_s, 1, QKV_OUT, H, x)                 # [T, 12288] fp32
+        att.copy_(cbmoe.ops.w8_linear(o_q, o_s, 1, H, QKV_OUT, qkv.to(torch.bfloat16)))
+        fetch.layer(layers[li], att, idx, w, LIMIT, out=out)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = launch_count()
+    with ClockSampler(0) as clocks:
+        ev0.record()
+        for s in range(args.steps):
+            step(args.warmup + s)
+        ev1.record()
+        torch.cuda.synchronize()
+    launches = launch_count() - l0
+    ms = ev0.elapsed_time(ev1) / args.steps
+    profile_read(reset=True)
+    profile_enable(True)
+    for s in range(args.steps):
+        step(args.warmup + s)
+    torch.cuda.synchronize()
+    profile_enable(False)
+    prof = profile_read(reset=True)
+    S = T_PREFILL * TOPK
+    flops = {"grp_cb3_gateup": 2.0 * S * 2 * H * I, "grp_cb3_down": 2.0 * S * H * I,
+             "grp_w8_gateup": 2.0 * T_PREFILL * 2 * H * I,
+             "grp_w8_store": 2.0 * T_PREFILL * H * I + 2 * 2.0 * T_PREFILL * H * QKV_OUT}
+    burst, sustained, kind = load_peaks_tc()
+    kern = {}
+    for name, f in flops.items():
+        if name in prof:
+            n, tms = prof[name]
+            per = f / (n / args.steps)        # flops per launch of this kind
+            kern[name] = {"launches": n, "avg_us": 1000 * tms / n, "tflops": per / (tms / n / 1000) / 1e12}
+    step_flops = sum(flops.values())
+    dom = "grp_cb3_gateup"
+    line = {"metric": METRIC, "value": T_PREFILL / (ms / 1000), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config3: MoE prefill layer, 4096 tokens, uniform top-8, E=160 CB3 + int8 shared, "
+                                   "+ int8 QKV 5120->12288 and O 12288->5120", "global_batch": T_PREFILL,
+                       "parallelism": "single GPU", "l2": "2 resident layers alternate (1.6 GB weights per step)"},
+            "clocks": clocks.summary(), "gpu_launches": launches,
+            "step_tflops": step_flops / (ms / 1000) / 1e12,
+            "roofline": {"bound": "tensor", "kernel": dom, "achieved": kern[dom]["tflops"], "peak": sustained,
+                         "unit": "TFLOP/s", "frac": kern[dom]["tflops"] / sustained,
+                         "peak_source": f"{kind} bf16_tflops_sustained (burst {burst})", "traffic": None},
+            "kernels": kern, "profile": {k: (v[0], round(v[1], 3)) for k, v in prof.items()}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.workload == "prefill" and args.impl == "ours":
+        run_prefill(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -3,16 +3,17 @@
 // (quant8.dequant_tree + dot, quant8.py:91-99).
 //
 //   D[w, t] = sum_k W_e[w, k] * X[t, k]     w: 128 weight rows of expert e (tcgen05 M = 128)
-//                                           t: up to 256 sorted token rows routed to e (tcgen05 N)
+//                                           t: up to 128 sorted token rows routed to e (tcgen05 N)
 // The weights are dequantized ONCE per (pass, 128-row tile) straight into the tensor core's shared-memory
 // operand layout; the tokens come in by TMA. One CTA per SM, 11 warps:
 //   warp 0       packed-weight producer: bulk copies of CB3K / W8K bits (+ codebooks / scales) into a ring
 //   warp 1       TMEM owner and MMA issuer (one thread): tcgen05.mma kind::f16, fp32 accumulators in TMEM
-//   warp 2       token producer: 2-D TMA loads of 256 x 64 bf16 tiles (128-byte swizzle)
+//   warp 2       token producer: 2-D TMA loads of 128 x 64 bf16 tiles (128-byte swizzle)
 //   warps 3-6    dequant: packed bits -> bf16 A tiles (the decode kernels' register dequant) -> shared memory
 //   warps 7-10   epilogue: tcgen05.ld of the accumulators -> SwiGLU (gate/up) or store -> bf16 rows
 // Barriers: per MMA stage full (4 dequant warps + token TMA) / empty (MMA commit); per packed slot full / empty;
-// tmem_full (MMA commit) / tmem_empty (4 epilogue warps). Every wait is bounded; a role that gives up sets
+// tmem_full[2] (MMA commit) / tmem_empty[2] (4 epilogue warps): two accumulator buffers, so the epilogue of one
+// item overlaps the MMAs of the next. Every wait is bounded; a role that gives up sets
 // CBMOE_DEVERR_TIMEOUT and falls through to the final barrier, after which warp 1 frees TMEM.
 // Items (pass, 128-row tile) are dealt round-robin to the persistent CTAs. No multicast anywhere.
 #include <cudaTypedefs.h>
@@ -29,7 +30,7 @@ namespace {
 constexpr int kGrpThreads = 11 * 32;
 constexpr int kWarpPk = 0, kWarpMma = 1, kWarpTok = 2, kWarpDq0 = 3, kWarpEpi0 = 7;
 
-template <int FMT, int NMAT>
+template <int FMT, int NMAT, int TN>
 struct GrpCfg {
   static constexpr int kGK = (FMT == kFmtCB3) ? kStageK : kChunkK;      // K per packed slot
   static constexpr int kChunks = kGK / kChunkK;                          // MMA stages per packed slot
@@ -38,31 +39,38 @@ struct GrpCfg {
   static constexpr int kPkData = 2 * kWarpsPerBlock * NMAT * kUnitSlice;
   static constexpr int kPkAux = (FMT == kFmtCB3) ? 2 * NMAT * 1024 : NMAT * kGrpTileM * 4;
   static constexpr int kPkBytes = kPkData + kPkAux;
-  static constexpr int kNpk = 2;
+  // CB3: one slot covers 4 MMA stages and the dequant warps free it as soon as its bits are in registers;
+  // W8: one slot per MMA stage, so several are in flight
+  static constexpr int kNpk = (FMT == kFmtCB3) ? 1 : 3;
   static constexpr int kATile = kGrpTileM * 128;                         // 16 KB: 128 rows x 64 bf16
-  static constexpr int kBTile = kGrpTileN * 128;                         // 32 KB
+  static constexpr int kBTile = TN * 128;                                // 16 / 32 KB
   static constexpr int kStage = NMAT * kATile + kBTile;
-  static constexpr int kNStage = (NMAT == 2) ? 2 : 3;
-  static constexpr int kTmemCols = NMAT * 256;
+  static constexpr int kNStage = (FMT == kFmtW8) ? ((NMAT == 2 || TN == 256) ? 3 + (TN == 256) : 5)
+                                                 : ((NMAT == 2) ? 4 : 6);
+  static constexpr int kAccCols = NMAT * TN;                             // one accumulator buffer
+  static constexpr int kTmemCols = 2 * kAccCols;                         // double-buffered
   static constexpr int kBarOff = kNStage * kStage + kNpk * kPkBytes;
   static constexpr int kSmem = 1024 + kBarOff + 256;                     // +1024: manual 1 KB alignment
+  static_assert(kSmem <= 227 * 1024, "shared memory budget");
 };
 
 struct ItemInfo {
   int e, row0, cnt, rt;
 };
 
+template <int TN>
 __device__ __forceinline__ int grp_n_items(const GroupedParams& p) {
-  const int np = p.pass_expert ? *p.n_pass : (p.N + kGrpTileN - 1) / kGrpTileN;
+  const int np = p.pass_expert ? *p.n_pass : (p.N + TN - 1) / TN;
   return np * (p.rows / kGrpTileM);
 }
 
+template <int TN>
 __device__ __forceinline__ ItemInfo grp_item(const GroupedParams& p, int item) {
   const int RT = p.rows / kGrpTileM;
   const int pass = item / RT, rt = item % RT;
   if (p.pass_expert == nullptr) {
-    const int row0 = pass * kGrpTileN;
-    return {0, row0, min(kGrpTileN, p.N - row0), rt};
+    const int row0 = pass * TN;
+    return {0, row0, min(TN, p.N - row0), rt};
   }
   return {p.pass_expert[pass], p.pass_row0[pass], p.pass_cnt[pass], rt};
 }
@@ -71,10 +79,10 @@ __device__ __forceinline__ bool item_ok(const GroupedParams& p, const ItemInfo& 
   return it.e >= 0 && it.e < p.E && it.cnt > 0;
 }
 
-template <int FMT, int NMAT, int EPI>
+template <int FMT, int NMAT, int EPI, int TN>
 __global__ void __launch_bounds__(kGrpThreads, 1) grouped_kernel(const GroupedParams p,
                                                                  const __grid_constant__ CUtensorMap tmap_b) {
-  using C = GrpCfg<FMT, NMAT>;
+  using C = GrpCfg<FMT, NMAT, TN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
@@ -84,9 +92,9 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grouped_kernel(const GroupedPa
   uint64_t* empty = full + C::kNStage;
   uint64_t* pk_full = empty + C::kNStage;
   uint64_t* pk_empty = pk_full + C::kNpk;
-  uint64_t* tm_full = pk_empty + C::kNpk;
-  uint64_t* tm_empty = tm_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tm_empty + 1);
+  uint64_t* tm_full = pk_empty + C::kNpk;     // [2]
+  uint64_t* tm_empty = tm_full + 2;           // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tm_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -98,8 +106,10 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grouped_kernel(const GroupedPa
       mbar_init(&pk_full[s], 1);
       mbar_init(&pk_empty[s], kWarpsPerBlock);
     }
-    mbar_init(tm_full, 1);
-    mbar_init(tm_empty, kWarpsPerBlock);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tm_full[b], 1);
+      mbar_init(&tm_empty[b], kWarpsPerBlock);
+    }
     fence_mbar_init();
   }
   if (warp == kWarpMma) tmem_alloc(tmem_slot, C::kTmemCols);
@@ -109,7 +119,7 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grouped_kernel(const GroupedPa
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  const int n_items = grp_n_items(p);
+  const int n_items = grp_n_items<TN>(p);
   const int RB = p.rows / kRowsPerBlock, KS256 = p.K / kStageK, KS64 = p.K / kChunkK;
   const int KG = p.K / C::kGK;
 
@@ -118,7 +128,7 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grouped_kernel(const GroupedPa
     int ps = 0;
     uint32_t pph = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-      const ItemInfo it = grp_item(p, item);
+      const ItemInfo it = grp_item<TN>(p, item);
       if (!item_ok(p, it)) continue;
       for (int kg = 0; kg < KG; ++kg) {
         const bool first = kg == 0;
@@ -170,7 +180,7 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grouped_kernel(const GroupedPa
       int st = 0;
       uint32_t ph = 0;
       for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const ItemInfo it = grp_item(p, item);
+        const ItemInfo it = grp_item<TN>(p, item);
         if (!item_ok(p, it)) continue;
         for (int ks = 0; ks < KS64; ++ks) {
           if (!mbar_wait_sleepy(&empty[st], ph ^ 1)) goto done;
@@ -189,11 +199,13 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grouped_kernel(const GroupedPa
       int st = 0;
       uint32_t ph = 0, local = 0;
       for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const ItemInfo it = grp_item(p, item);
+        const ItemInfo it = grp_item<TN>(p, item);
         if (!item_ok(p, it)) continue;
         const int n = (it.cnt + 15) & ~15;
         const uint32_t idesc = idesc_bf16_m128(n);
-        if (!mbar_wait(tm_empty, (local & 1) ^ 1)) goto done;
+        const int buf = local & 1;
+        const uint32_t acc = tmem + buf * C::kAccCols;
+        if (!mbar_wait(&tm_empty[buf], ((local >> 1) & 1) ^ 1)) goto done;
         tc_fence_after();
         for (int ks = 0; ks < KS64; ++ks) {
           if (!mbar_wait(&full[st], ph)) goto done;
@@ -205,7 +217,7 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grouped_kernel(const GroupedPa
 #pragma unroll
             for (int m = 0; m < NMAT; ++m) {
               const uint64_t adesc = sw128_desc(sbase + m * C::kATile);
-              umma_bf16(tmem + m * 256, adesc + 2 * kk, bdesc + 2 * kk, idesc, (ks | kk) != 0);
+              umma_bf16(acc + m * TN, adesc + 2 * kk, bdesc + 2 * kk, idesc, (ks | kk) != 0);
             }
           }
           umma_commit(&empty[st]);
@@ -214,7 +226,7 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grouped_kernel(const GroupedPa
             ph ^= 1;
           }
         }
-        umma_commit(tm_full);
+        umma_commit(&tm_full[buf]);
         ++local;
       }
     }
@@ -227,7 +239,7 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grouped_kernel(const GroupedPa
     Codebook cbg[2][NMAT], cbh[2][NMAT];
     float sg[2][NMAT], sh[2][NMAT];
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-      const ItemInfo it = grp_item(p, item);
+      const ItemInfo it = grp_item<TN>(p, item);
       if (!item_ok(p, it)) continue;
       for (int kg = 0; kg < KG; ++kg) {
         if (!mbar_wait(&pk_full[ps], pph)) goto done;
@@ -330,17 +342,18 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grouped_kernel(const GroupedPa
     const int q = warp & 3;              // TMEM lane quadrant this warp may read
     uint32_t local = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-      const ItemInfo it = grp_item(p, item);
+      const ItemInfo it = grp_item<TN>(p, item);
       if (!item_ok(p, it)) continue;
-      if (!mbar_wait(tm_full, local & 1)) goto done;
+      const int buf = local & 1;
+      if (!mbar_wait(&tm_full[buf], (local >> 1) & 1)) goto done;
       tc_fence_after();
       const int wrow = it.rt * kGrpTileM + 32 * q + lane;
-      const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16);
+      const uint32_t tbase = tmem + buf * C::kAccCols + ((uint32_t)(32 * q) << 16);
       const int n = (it.cnt + 15) & ~15;
       for (int c0 = 0; c0 < n; c0 += 16) {
         float v0[16], v1[16];
         tmem_ld16(tbase + c0, v0);
-        if constexpr (NMAT == 2) tmem_ld16(tbase + 256 + c0, v1);
+        if constexpr (NMAT == 2) tmem_ld16(tbase + TN + c0, v1);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           if (c0 + j < it.cnt) {
@@ -357,7 +370,7 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grouped_kernel(const GroupedPa
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(tm_empty);
+      if (lane == 0) mbar_arrive(&tm_empty[buf]);
       ++local;
     }
   }
@@ -385,13 +398,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// bf16 matrix [rows][K] (row stride K*2 bytes): 64 x 256 boxes, 128-byte swizzle, zero fill out of bounds.
-int make_token_map(CUtensorMap* map, const void* base, int K, int rows) {
+// bf16 matrix [rows][K] (row stride K*2 bytes): 64 x 128 boxes, 128-byte swizzle, zero fill out of bounds.
+int make_token_map(CUtensorMap* map, const void* base, int K, int rows, int box_rows) {
   auto fn = encode_fn();
   if (fn == nullptr) return CBMOE_ERR_CUDA;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kChunkK, (cuuint32_t)kGrpTileN};
+  const cuuint32_t box[2] = {(cuuint32_t)kChunkK, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -399,15 +412,15 @@ int make_token_map(CUtensorMap* map, const void* base, int K, int rows) {
   return r == CUDA_SUCCESS ? CBMOE_OK : CBMOE_ERR_CUDA;
 }
 
-template <int FMT, int NMAT, int EPI>
+template <int FMT, int NMAT, int EPI, int TN>
 int launch_grouped(const GroupedParams& p, const void* b, int b_rows, int kind, cudaStream_t stream) {
-  using C = GrpCfg<FMT, NMAT>;
+  using C = GrpCfg<FMT, NMAT, TN>;
   if (p.rows % kGrpTileM || p.K % kStageK || b_rows <= 0 || (reinterpret_cast<uintptr_t>(b) & 15))
     return CBMOE_ERR_INVALID;
   CUtensorMap map;
-  int rc = make_token_map(&map, b, p.K, b_rows);
+  int rc = make_token_map(&map, b, p.K, b_rows, TN);
   if (rc) return rc;
-  auto kern = grouped_kernel<FMT, NMAT, EPI>;
+  auto kern = grouped_kernel<FMT, NMAT, EPI, TN>;
   static bool attr = false;
   if (!attr) {
     CBMOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
@@ -433,18 +446,30 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ x, int H16, const i
 }
 
 // out[n][r] = add[n][r] + sum_j w[n][j] * y_sorted[row_slot[n][j]][r], y_sorted / add bf16; fp32 or bf16 out.
+// One thread per 8 consecutive outputs (16-byte loads of the bf16 rows).
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
 __global__ void combine_bf16_kernel(const uint16_t* __restrict__ y_sorted, const int* __restrict__ row_slot,
                                     const float* __restrict__ wts, int N, int topk, int H,
                                     const uint16_t* __restrict__ add, float* __restrict__ out_f32,
                                     uint16_t* __restrict__ out_bf16) {
-  const long long total = (long long)N * H;
+  const int H8 = H / 8;
+  const long long total = (long long)N * H8;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
-    const int n = (int)(i / H), r = (int)(i % H);
-    float v = 0.f;
+    const int n = (int)(i / H8), c8 = (int)(i % H8);
+    float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int q0 = 0; q0 < topk; q0 += 8) {
       int rs[8];
-      float wt[8], yy[8];
+      float wt[8];
+      uint4 yv[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const bool in = q0 + q < topk;
@@ -452,23 +477,30 @@ __global__ void combine_bf16_kernel(const uint16_t* __restrict__ y_sorted, const
         wt[q] = in ? wts[n * topk + q0 + q] : 0.f;
       }
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        if (rs[q] >= 0) {
-          const uint16_t b = y_sorted[(size_t)rs[q] * H + r];
-          yy[q] = __uint_as_float((uint32_t)b << 16);
-        } else {
-          yy[q] = 0.f;
-        }
-      }
+      for (int q = 0; q < 8; ++q)
+        yv[q] = rs[q] >= 0 ? reinterpret_cast<const uint4*>(y_sorted + (size_t)rs[q] * H)[c8] : make_uint4(0, 0, 0, 0);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) v += wt[q] * yy[q];
+      for (int q = 0; q < 8; ++q) {
+        float f[8];
+        bf16x8_to_f32(yv[q], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] += wt[q] * f[e];
+      }
     }
-    if (add != nullptr) v += __uint_as_float((uint32_t)add[i] << 16);
-    if (out_f32 != nullptr) out_f32[i] = v;
-    if (out_bf16 != nullptr) {
-      const __nv_bfloat16 o = __float2bfloat16_rn(v);
-      out_bf16[i] = *reinterpret_cast<const uint16_t*>(&o);
+    if (add != nullptr) {
+      float f[8];
+      bf16x8_to_f32(reinterpret_cast<const uint4*>(add + (size_t)n * H)[c8], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] += f[e];
     }
+    const size_t o = (size_t)n * H + (size_t)c8 * 8;
+    if (out_f32 != nullptr) {
+      reinterpret_cast<float4*>(out_f32 + o)[0] = make_float4(v[0], v[1], v[2], v[3]);
+      reinterpret_cast<float4*>(out_f32 + o)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    if (out_bf16 != nullptr)
+      *reinterpret_cast<uint4*>(out_bf16 + o) =
+          make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
   }
 }
 
@@ -481,19 +513,19 @@ int grid_of(long long total) {
 }  // namespace
 
 int grouped_cb3_gateup(const GroupedParams& p, const void* b, int b_rows, cudaStream_t s) {
-  return launch_grouped<kFmtCB3, 2, kGrpEpiSwiglu>(p, b, b_rows, kProfGrpCb3GateUp, s);
+  return launch_grouped<kFmtCB3, 2, kGrpEpiSwiglu, kGrpTileN>(p, b, b_rows, kProfGrpCb3GateUp, s);
 }
 int grouped_cb3_down(const GroupedParams& p, const void* b, int b_rows, cudaStream_t s) {
-  return launch_grouped<kFmtCB3, 1, kGrpEpiStore>(p, b, b_rows, kProfGrpCb3Down, s);
+  return launch_grouped<kFmtCB3, 1, kGrpEpiStore, kGrpTileN>(p, b, b_rows, kProfGrpCb3Down, s);
 }
 int grouped_w8_gateup(const GroupedParams& p, const void* b, int b_rows, cudaStream_t s) {
-  return launch_grouped<kFmtW8, 2, kGrpEpiSwiglu>(p, b, b_rows, kProfGrpW8GateUp, s);
+  return launch_grouped<kFmtW8, 2, kGrpEpiSwiglu, 128>(p, b, b_rows, kProfGrpW8GateUp, s);
 }
 int grouped_w8_store(const GroupedParams& p, const void* b, int b_rows, cudaStream_t s) {
-  return launch_grouped<kFmtW8, 1, kGrpEpiStore>(p, b, b_rows, kProfGrpW8Store, s);
+  return launch_grouped<kFmtW8, 1, kGrpEpiStore, 256>(p, b, b_rows, kProfGrpW8Store, s);
 }
 int grouped_w8_store_f32(const GroupedParams& p, const void* b, int b_rows, cudaStream_t s) {
-  return launch_grouped<kFmtW8, 1, kGrpEpiStoreF32>(p, b, b_rows, kProfGrpW8Store, s);
+  return launch_grouped<kFmtW8, 1, kGrpEpiStoreF32, 256>(p, b, b_rows, kProfGrpW8Store, s);
 }
 
 int launch_gather_rows(const uint16_t* x, int H, const int* tok_row, int rows, uint16_t* xs, cudaStream_t s) {
@@ -509,7 +541,7 @@ int launch_gather_rows(const uint16_t* x, int H, const int* tok_row, int rows, u
 int launch_combine_bf16(const uint16_t* y_sorted, const int* row_slot, const float* wts, int N, int topk, int H,
                         const uint16_t* add_bf16, float* out_f32, uint16_t* out_bf16, cudaStream_t s) {
   prof_begin(kProfCombine, s);
-  combine_bf16_kernel<<<grid_of((long long)N * H), 256, 0, s>>>(y_sorted, row_slot, wts, N, topk, H, add_bf16, out_f32,
+  combine_bf16_kernel<<<grid_of((long long)N * H / 8), 256, 0, s>>>(y_sorted, row_slot, wts, N, topk, H, add_bf16, out_f32,
                                                                  out_bf16);
   prof_end(kProfCombine, s);
   CBMOE_CUDA_TRY(cudaGetLastError());

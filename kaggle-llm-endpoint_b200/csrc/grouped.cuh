@@ -10,7 +10,7 @@ constexpr int kGrpEpiSwiglu = 0;   // NMAT = 2: out = bf16(swiglu_clamped(gate, 
 constexpr int kGrpEpiStore = 1;    // NMAT = 1: out = bf16(acc)
 constexpr int kGrpEpiStoreF32 = 2; // NMAT = 1: out_f32 = acc
 constexpr int kGrpTileM = 128;     // weight rows per tile (tcgen05 M)
-constexpr int kGrpTileN = 256;     // token rows per pass (max tcgen05 N)
+constexpr int kGrpTileN = 128;     // token rows per pass (tcgen05 N); two accumulator buffers fit TMEM
 
 struct GroupedParams {
   const uint8_t* wq;       // CB3K index bits or W8K int8, unit layout (layout.cuh)
