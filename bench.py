@@ -17,7 +17,9 @@ ranks); e2e = the same through the public API with pinned host inputs copied in 
 every step; roofline = the dominant kernel's algorithmic bytes / its event-timed duration vs the measured HBM copy
 peak; cpu_baseline = the C oracle (OpenMP) on a bounded sample of the same workload on this host's cores.
 --impl reference times that CPU restatement alone (the reference's own path is JAX-on-TPU and cannot run here).
-N > 1: every rank runs the same workload on its own GPU as an independent replica (scaling "weak").
+N > 1: expert parallelism, config 1 per GPU: each rank owns 8 tokens and E/N of the 160 experts of every layer;
+a step routes all ranks' slots to the ranks holding their experts (NCCL send/recv), computes, returns and combines
+(scaling "weak": 8 tokens per GPU at every N; `value` = all ranks' tokens / the slowest rank's time).
 """
 import argparse
 import json
@@ -28,6 +30,10 @@ import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+# stdout carries exactly one JSON line: NCCL's log (its version banner included) goes to stderr
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+if os.environ.get("NCCL_DEBUG", "").upper() in ("VERSION", "WARN"):
+    del os.environ["NCCL_DEBUG"]
 PKG = os.path.join(ROOT, "kaggle-llm-endpoint_b200")
 for _p in (ROOT, PKG):
     if _p not in sys.path:
@@ -62,7 +68,8 @@ def config_block(n_gpus):
             "topk": TOPK, "expert_format": "CB3 (3-bit indices, 8-entry bf16 codebook per row)",
             "shared_format": "int8 per-output-channel, fp32 scales",
             "l2": "inputs larger than L2: 16 resident layers (1.47 GB each) cycled, ~0.5 GB of fresh weights per step",
-            "parallelism": f"replicas x{n_gpus}" if n_gpus > 1 else "single GPU"}
+            "parallelism": f"expert parallel x{n_gpus} (NCCL dispatch/combine, 8 tokens per GPU)" if n_gpus > 1
+            else "single GPU"}
 
 
 # ------------------------------------------------------------------------------------------------ clocks
@@ -135,6 +142,25 @@ def make_layer(torch, cbmoe, seed, dev, keep_std=False):
     p = cbmoe.pack_layer(gate, up, down, shared)
     std = {"gate": gate, "up": up, "down": down, "shared": shared} if keep_std else None
     return p, std
+
+
+def make_layer_tables(torch, seed, dev):
+    """Unpacked CB3 tables + int8 shared expert of one layer (the same from every rank for a given seed)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+
+    def cb3(rows, K):
+        words = torch.randint(0, 256, (E * rows * K * 3 // 32 * 4,), dtype=torch.uint8, device=dev, generator=g)
+        cb = (torch.randn((E, rows, 8), device=dev, generator=g) * 0.02).to(torch.bfloat16).float()
+        return words.view(torch.int32).view(E, rows, K * 3 // 32), cb.sort(dim=-1).values.to(torch.bfloat16)
+
+    def q8(n_in, n_out):
+        w = torch.randn((n_in, n_out), device=dev, generator=g) * 0.02
+        s = torch.clamp(w.abs().amax(dim=0, keepdim=True), min=1e-12) / 127.0
+        return torch.clamp(torch.round(w / s), -127, 127).to(torch.int8), s
+
+    tables = (cb3(I, H), cb3(I, H), cb3(H, I), (q8(H, I), q8(H, I), q8(I, H)))
+    return tables, None
 
 
 def make_batches(torch, dev, seed, n_batches):
@@ -296,18 +322,33 @@ def run_ours(args):
 
     layers, std0 = [], None
     n_layers = max(1, args.layers)
-    for li in range(n_layers):
-        p, std = make_layer(torch, cbmoe, 1000 + li + 100 * rank, dev, keep_std=(li == 0 and rank == 0))
-        layers.append(p)
-        std0 = std0 or std
+    group = None
+    if world > 1:
+        # expert parallel: every rank generates each layer from the same seed and keeps its E/world experts
+        from cbmoe.ep import ExpertParallel
+        group = ExpertParallel()
+        for li in range(n_layers):
+            full, std = make_layer_tables(torch, 1000 + li, dev)
+            layers.append(group.pack_local(*full))
+            del full, std
+    else:
+        for li in range(n_layers):
+            p, std = make_layer(torch, cbmoe, 1000 + li, dev, keep_std=(li == 0))
+            layers.append(p)
+            std0 = std0 or std
     batches = make_batches(torch, dev, 7 + rank, N_BATCHES)
     fetch = cbmoe.ResidentFetch(path="decode")
     out = torch.empty((N_TOK, H), dtype=torch.bfloat16, device=dev)
+    # rows per peer in each direction: 4x the mean share of a rank's slots (uniform routing), at least 16
+    cap = min(N_TOK * TOPK, max(16, 4 * N_TOK * TOPK // max(world, 1)))
     torch.cuda.synchronize()
 
     def step(s):
         x, idx, w = batches[s % N_BATCHES]
-        fetch.layer(layers[s % n_layers], x, idx, w, LIMIT, out=out)
+        if group is not None:
+            group.layer(layers[s % n_layers], x, idx, w, LIMIT, capacity=cap, out=out)
+        else:
+            fetch.layer(layers[s % n_layers], x, idx, w, LIMIT, out=out)
 
     def barrier():
         if world > 1:
@@ -350,7 +391,10 @@ def run_ours(args):
         xd.copy_(xh, non_blocking=True)
         idd.copy_(ih, non_blocking=True)
         wd.copy_(wh, non_blocking=True)
-        fetch.layer(layers[s % n_layers], xd, idd, wd, LIMIT, out=out)
+        if group is not None:
+            group.layer(layers[s % n_layers], xd, idd, wd, LIMIT, capacity=cap, out=out)
+        else:
+            fetch.layer(layers[s % n_layers], xd, idd, wd, LIMIT, out=out)
         out_h.copy_(out, non_blocking=True)
 
     for s in range(args.warmup):
@@ -378,7 +422,16 @@ def run_ours(args):
     torch.cuda.synchronize()
     profile_enable(False)
     prof = profile_read(reset=True)
-    n_unique = [int(torch.unique(idx).numel()) for _, idx, _ in batches]
+    if group is not None:      # experts this rank serves: distinct ids of ALL ranks' tokens that fall in its range
+        lo, hi = group.expert_range(E)
+        n_unique = []
+        for _, idx, _ in batches:
+            allidx = [torch.empty_like(idx) for _ in range(world)]
+            dist.all_gather(allidx, idx)
+            u = torch.unique(torch.cat(allidx))
+            n_unique.append(int(((u >= lo) & (u < hi)).sum().item()))
+    else:
+        n_unique = [int(torch.unique(idx).numel()) for _, idx, _ in batches]
     uniq = [n_unique[(args.warmup + s) % N_BATCHES] for s in range(args.steps)]
     S = N_TOK * TOPK
     gateup_bytes = sum(u * (2 * I * H * 3 // 8 + 2 * I * 16) + N_TOK * H * 2 + S * I * 4 for u in uniq)
@@ -435,6 +488,7 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        group.close()
         dist.destroy_process_group()
 
 

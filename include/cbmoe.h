@@ -31,7 +31,8 @@ extern "C" {
 #define CBMOE_ERR_DEVICE (-6)      /* a kernel recorded a device-side error (cbmoe_device_errors) */
 
 #define CBMOE_DEVERR_TIMEOUT 1     /* a bounded spin-wait gave up */
-#define CBMOE_DEVERR_INDEX 2       /* an expert id outside [0, E) was routed (the slot is skipped) */
+#define CBMOE_DEVERR_INDEX 2       /* an expert id >= E was routed (the slot is skipped); ids < 0 are empty slots */
+#define CBMOE_DEVERR_CAPACITY 4    /* expert parallel: more slots for one peer than the capacity (extra dropped) */
 
 #define CBMOE_PATH_AUTO 0          /* decode kernel for small batches, grouped tensor-core GEMM otherwise */
 #define CBMOE_PATH_DECODE 1        /* fused dequant matvec (resident.py:110-120 `_apply_kernel`) */
@@ -120,7 +121,8 @@ typedef struct cbmoe_shared {
 /* Workspace bytes for cbmoe_experts_apply / cbmoe_moe_layer with N tokens and top-k routing. */
 size_t cbmoe_workspace_bytes(const cbmoe_experts* ex, int N, int k, int path);
 
-/* ResidentFetch.apply (resident.py:100-108): x bf16 [N, H], idx int32 [N, k] in [0, E), w fp32 [N, k] ->
+/* ResidentFetch.apply (resident.py:100-108): x bf16 [N, H], idx int32 [N, k] in [0, E) (negative = empty slot),
+ * w fp32 [N, k] ->
  * y fp32 [N, H] = sum_j w[n, j] * down_e(swiglu_clamped(gate_e x_n, up_e x_n, limit)), e = idx[n, j]. */
 int cbmoe_experts_apply(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx, const float* w,
                         int k, float limit, int path, float* y, void* workspace, size_t workspace_bytes,
@@ -155,6 +157,22 @@ int cbmoe_cb3_matvec(const void* idx_k, const void* cb_k, int rows, int K, const
  * y fp32 [N, rows] = x @ bf16(q * s). Workspace: cbmoe_matvec_workspace_bytes. */
 int cbmoe_w8_linear(const void* qk, const float* s, int scale_axis, int rows, int K, const uint16_t* x, int N,
                     float* y, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* -------------------------------------------------------------------------------- expert parallelism
+ * Routed experts sharded by id over the ranks of one node (rank r holds experts [r*E/n, (r+1)*E/n)); tokens stay on
+ * their rank; the shared expert is replicated. The reference shards moe_inter instead (engine.py:129-176) and
+ * psums the partials (model.py:855); the EP layer's output equals the single-GPU layer's (model.py:840-856).
+ * Communicator: rank 0 calls cbmoe_ep_unique_id, the 128 bytes reach every rank out of band, each rank calls
+ * cbmoe_ep_comm_init (NCCL, blocking). cbmoe_ep_layer is stream-ordered on `stream` (NCCL send/recv included);
+ * `capacity` = rows per peer in each direction: a rank sends at most `capacity` slots to one peer, the rest are
+ * dropped and flagged CBMOE_DEVERR_CAPACITY (N_local * k is always enough). local: this rank's E/n experts. */
+int cbmoe_ep_unique_id(uint8_t* id128_host);
+int cbmoe_ep_comm_init(const uint8_t* id128_host, int nranks, int rank, void** comm_out);
+int cbmoe_ep_comm_destroy(void* comm);
+size_t cbmoe_ep_workspace_bytes(const cbmoe_experts* local, int N_local, int k, int nranks, int capacity);
+int cbmoe_ep_layer(void* comm, int nranks, int rank, const cbmoe_experts* local, int E_total, const cbmoe_shared* sh,
+                   const uint16_t* x, int N_local, const int32_t* idx, const float* w, int k, float limit,
+                   int capacity, uint16_t* out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,84 @@
+"""Expert parallelism over the GPUs of one node (one process per GPU, torch.distributed for the plumbing).
+
+    group = ExpertParallel()                                    # after torch.distributed.init_process_group
+    local = group.pack_local(gate, up, down, shared)            # this rank's E/n experts (+ replicated shared)
+    out = group.layer(local, x, idx, w, limit)                  # tokens of this rank -> bf16 [N_local, H]
+
+The routed experts are sharded by id (rank r holds [r*E/n, (r+1)*E/n)); every rank keeps its tokens. One layer
+call routes each (token, slot) to the rank holding its expert, exchanges rows with NCCL send/recv over NVLink,
+runs the local experts on what it received, sends the outputs back and combines them with the shared expert
+(include/cbmoe.h, cbmoe_ep_layer). The NCCL communicator is the library's own, bootstrapped through the
+torch.distributed process group (rank 0's NCCL unique id is broadcast).
+"""
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from ._lib import Experts, Shared, check, lib, ptr, require_cuda, stream_handle
+
+
+class ExpertParallel:
+    def __init__(self, group=None):
+        self.rank = dist.get_rank(group)
+        self.nranks = dist.get_world_size(group)
+        idbuf = torch.zeros(128, dtype=torch.uint8)
+        if self.rank == 0:
+            raw = (ctypes.c_uint8 * 128)()
+            check(lib().cbmoe_ep_unique_id(raw), "cbmoe_ep_unique_id")
+            idbuf.copy_(torch.tensor(list(raw), dtype=torch.uint8))
+        dev = torch.device("cuda", torch.cuda.current_device())
+        if dist.get_backend(group) == "nccl":
+            t = idbuf.to(dev)
+            dist.broadcast(t, src=0, group=group)
+            idbuf = t.cpu()
+        else:
+            dist.broadcast(idbuf, src=0, group=group)
+        raw = (ctypes.c_uint8 * 128)(*idbuf.tolist())
+        comm = ctypes.c_void_p()
+        check(lib().cbmoe_ep_comm_init(raw, self.nranks, self.rank, ctypes.byref(comm)), "cbmoe_ep_comm_init")
+        self.comm = comm
+        self._ws = None
+
+    def close(self):
+        if self.comm:
+            check(lib().cbmoe_ep_comm_destroy(self.comm), "cbmoe_ep_comm_destroy")
+            self.comm = None
+
+    def expert_range(self, E):
+        assert E % self.nranks == 0, (E, self.nranks)
+        n = E // self.nranks
+        return self.rank * n, (self.rank + 1) * n
+
+    def pack_local(self, gate, up, down, shared):
+        """Full-layer CB3 tables (as for cbmoe.pack_layer) -> this rank's slice, packed; shared expert replicated."""
+        from .resident import pack_layer
+        E = gate[0].shape[0]
+        a, b = self.expert_range(E)
+        sl = lambda t: (t[0][a:b].contiguous(), t[1][a:b].contiguous())
+        p = pack_layer(sl(gate), sl(up), sl(down), shared)
+        p["E_total"] = E
+        return p
+
+    def layer(self, p, x, idx, w, limit, capacity=None, out=None):
+        """x bf16 [N_local, H], idx int32 [N_local, k] (global expert ids), w fp32 [N_local, k] -> bf16 [N_local, H].
+        `capacity` = rows per peer in each direction (default N_local * k: never drops)."""
+        require_cuda(x, idx, w)
+        N, k = idx.shape
+        cap = max(1, capacity if capacity is not None else N * k)
+        ex = Experts(p["E"], p["H"], p["I"], p["gate_up_q"][0].data_ptr(), p["gate_up_q"][1].data_ptr(),
+                     p["down_q"][0].data_ptr(), p["down_q"][1].data_ptr())
+        s = p["shared"]
+        sh = Shared(s["gate_up_q"].data_ptr(), s["gate_s"].data_ptr(), s["up_s"].data_ptr(), s["down_q"].data_ptr(),
+                    s["down_s"].data_ptr(), s["scale_axis"])
+        nbytes = lib().cbmoe_ep_workspace_bytes(ex, N, k, self.nranks, cap)
+        if self._ws is None or self._ws.numel() < nbytes:
+            self._ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+        if out is None:
+            out = torch.empty((N, p["H"]), dtype=torch.bfloat16, device=x.device)
+        xb = x.to(torch.bfloat16).contiguous()
+        check(lib().cbmoe_ep_layer(self.comm, self.nranks, self.rank, ex, p["E_total"], sh, ptr(xb), N,
+                                   ptr(idx.to(torch.int32).contiguous()), ptr(w.to(torch.float32).contiguous()), k,
+                                   float(limit), cap, ptr(out), ptr(self._ws), self._ws.numel(), stream_handle()),
+              "cbmoe_ep_layer")
+        return out

@@ -6,20 +6,18 @@
 
 #include "decode.cuh"
 #include "grouped.cuh"
+#include "layer.cuh"
 
 namespace cbmoe {
 
 __device__ int g_device_errors = 0;
 
-namespace {
+namespace lyr {
 thread_local int t_last_cuda_error = 0;
 
 constexpr size_t kAlign = 256;
 size_t align_up(size_t v) { return (v + kAlign - 1) & ~(kAlign - 1); }
 
-struct PlanLayoutHost {
-  int64_t off[14];
-};
 
 PlanLayoutHost host_plan_layout(int T, int k, int E, int tm, int pass_tokens) {
   PlanLayoutHost L;
@@ -27,30 +25,29 @@ PlanLayoutHost host_plan_layout(int T, int k, int E, int tm, int pass_tokens) {
   return L;
 }
 
-// Tokens per expert pass of the decode kernels for a batch of N tokens (each token picks an expert at most once).
+// Token tiles (of 8) per pass of the decode kernels. Shared expert: every token goes to the one expert, so by N.
 int decode_nt(int N) { return N <= 8 ? 1 : (N <= 16 ? 2 : 4); }
+// Routed experts: by the average slots per expert (an expert with more tokens than a pass takes several passes;
+// larger passes cost shared memory and occupancy on every item).
+int decode_nt_routed(int N, int k, int E) {
+  const long long S = (long long)N * k;
+  return S <= 2LL * E ? 1 : (S <= 6LL * E ? 2 : 4);
+}
 
 // Workspace of the decode path:
 //   plan | h (Rp x 2I bf16) | y_sorted (Rp x H f32) | h_shared (N x 2I bf16) |
 //   scheduling words: routed [gate/up next, down next, gate/up split counters...] (zeroed by the plan kernel),
 //                     shared [gate/up next, down next, split counters...] (zeroed by a memset on the side stream) |
 //   split-K partial sums of the routed gate/up, the shared gate/up and the shared down.
-struct DecodeWorkspace {
-  size_t plan, h, y, hs, sched, part_gu, part_sgu, part_sdn, total;
-  int nt, Rp, P, Ps, RB_gu, RB_dn;
-  int kq_gu, kq_sgu, kq_sdn;
-  int n_zero_routed, n_zero_shared;   // words
-  PlanLayoutHost L;
-};
 
 DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k) {
   DecodeWorkspace w;
-  w.nt = decode_nt(N);
+  w.nt = decode_nt_routed(N, k, E);
   const int pt = 8 * w.nt;
   w.L = host_plan_layout(N, k, E, 1, pt);
   w.Rp = (int)(w.L.off[8] - w.L.off[7]);
   w.P = (int)(w.L.off[11] - w.L.off[10]);
-  w.Ps = (N + pt - 1) / pt;
+  w.Ps = (N + 8 * decode_nt(N) - 1) / (8 * decode_nt(N));   // shared-expert passes
   w.RB_gu = I / kRowsPerBlock;
   w.RB_dn = H / kRowsPerBlock;
   const int KS_gu = H / kStageK, KS_dn = I / kStageK;
@@ -97,10 +94,6 @@ DecodeParams base_params() {
 // Per host thread and device: a second stream and two events, so the shared expert's gate/up (independent of
 // the routing) runs concurrently with the routed experts: fork after the caller's prior work, join before the
 // shared down + combine. Created on first use; stream-ordered, so the sequence also records into a graph capture.
-struct SideStream {
-  cudaStream_t s = nullptr;
-  cudaEvent_t fork = nullptr, join = nullptr;
-};
 thread_local SideStream t_side[64];
 
 int side_stream(SideStream** out) {
@@ -184,11 +177,6 @@ int pick_path(int N, int k, int path) {
 
 // Workspace of the grouped path: plan | xs (Rp x H bf16, tokens gathered in expert order) | h (Rp x I bf16) |
 // y_sorted (Rp x H bf16) | shared h (N x I bf16) | shared down (N x H bf16).
-struct GroupedWorkspace {
-  size_t plan, xs, h, y, hs, sy, total;
-  int Rp;
-  PlanLayoutHost L;
-};
 
 GroupedWorkspace grouped_workspace(int E, int H, int I, int N, int k) {
   GroupedWorkspace w;
@@ -238,7 +226,8 @@ int routed_grouped(const cbmoe_experts* ex, const uint16_t* x, int N, const int3
   return grouped_cb3_down(d, h, W.Rp, stream);
 }
 
-}  // namespace
+}  // namespace lyr
+using namespace lyr;
 
 void set_last_cuda_error(cudaError_t e) { t_last_cuda_error = (int)e; }
 

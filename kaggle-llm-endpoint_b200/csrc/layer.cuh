@@ -1,0 +1,52 @@
+// Internal interface between the C-ABI files (capi.cu, ep.cu): workspace layouts and the routed-expert kernel
+// sequences of one layer call. Not part of the public ABI.
+#pragma once
+#include "decode.cuh"
+#include "grouped.cuh"
+
+namespace cbmoe {
+namespace lyr {
+
+struct PlanLayoutHost {
+  int64_t off[14];
+};
+
+// Workspace of the decode path (layout documented at decode_workspace in capi.cu).
+struct DecodeWorkspace {
+  size_t plan, h, y, hs, sched, part_gu, part_sgu, part_sdn, total;
+  int nt, Rp, P, Ps, RB_gu, RB_dn;
+  int kq_gu, kq_sgu, kq_sdn;
+  int n_zero_routed, n_zero_shared;   // words
+  PlanLayoutHost L;
+};
+
+struct GroupedWorkspace {
+  size_t plan, xs, h, y, hs, sy, total;
+  int Rp;
+  PlanLayoutHost L;
+};
+
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+size_t align_up(size_t v);
+PlanLayoutHost host_plan_layout(int T, int k, int E, int tm, int pass_tokens);
+int decode_nt(int N);
+int decode_nt_routed(int N, int k, int E);
+DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k);
+GroupedWorkspace grouped_workspace(int E, int H, int I, int N, int k);
+int pick_path(int N, int k, int path);
+bool aligned16(const void* p);
+bool experts_ok(const cbmoe_experts* ex);
+bool shared_ok(const cbmoe_shared* sh);
+DecodeParams base_params();
+int side_stream(SideStream** out);
+int routed_decode(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx, const float* w, int k,
+                  float limit, uint8_t* ws, const DecodeWorkspace& W, cudaStream_t stream);
+int routed_grouped(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx, const float* w, int k,
+                   float limit, uint8_t* ws, const GroupedWorkspace& W, cudaStream_t stream);
+
+}  // namespace lyr
+}  // namespace cbmoe

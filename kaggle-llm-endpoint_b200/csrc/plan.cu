@@ -84,10 +84,11 @@ __global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(const int32_t*
   for (int base = beg; base < end; base += 32) {
     const int s = base + lane;
     int e = (s < end) ? idx[s] : -1;
-    if (s < end && (e < 0 || e >= E)) {
+    if (s < end && e >= E) {          // negative ids are empty slots; ids past E are errors
       atomicOr(&g_device_errors, CBMOE_DEVERR_INDEX);
       e = -1;
     }
+    if (e < 0) e = -1;
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * E + e] += __popc(peers);
   }
@@ -197,7 +198,7 @@ __global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(const int32_t*
   for (int base = beg; base < end; base += 32) {
     const int s = base + lane;
     int e = (s < end) ? idx[s] : -1;
-    if (e >= E) e = -1;
+    if (e >= E || e < 0) e = -1;
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     int pos = -1;
     if (e >= 0) {
@@ -238,10 +239,11 @@ __device__ __forceinline__ void chunk_warp_counts(const int32_t* idx, int beg, i
   for (int base = beg; base < end; base += 32) {
     const int s = base + lane;
     int e = (s < end) ? idx[s] : -1;
-    if (s < end && (e < 0 || e >= E)) {
+    if (s < end && e >= E) {          // negative ids are empty slots; ids past E are errors
       if (flag_errors) atomicOr(&g_device_errors, CBMOE_DEVERR_INDEX);
       e = -1;
     }
+    if (e < 0) e = -1;
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * E + e] += __popc(peers);
   }
@@ -409,7 +411,7 @@ __global__ void __launch_bounds__(kPlanCtaWarps * 32) plan_place_kernel(const in
   for (int base = beg; base < end; base += 32) {
     const int s = base + lane;
     int e = (s < end) ? idx[s] : -1;
-    if (e >= E) e = -1;
+    if (e >= E || e < 0) e = -1;
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     int pos = -1;
     if (e >= 0) {
