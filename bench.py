@@ -444,7 +444,7 @@ def run_ours(args):
             n, tms = prof[name]
             kern[name] = {"launches": n, "avg_us": 1000 * tms / n, "gbs": nbytes / (tms / 1000) / 1e9,
                           "bytes_per_launch": nbytes / n}
-    for name in ("plan", "w8_gateup", "w8_down_combine"):
+    for name in ("plan", "w8_gateup", "w8_down", "combine"):
         if name in prof:
             n, tms = prof[name]
             kern[name] = {"launches": n, "avg_us": 1000 * tms / n}

@@ -137,7 +137,7 @@ int cbmoe_experts_apply(const cbmoe_experts* ex, const uint16_t* x, int N, const
  * intermediate 1536, top-8: up to 64 tokens fit). The first call on a device looks up the array's device address
  * (make it before any stream capture). All calls on a device share the array: calls that overlap on the GPU race.
  * Allocates nothing: no cudaMalloc, cudaFree or allocating library call. */
-#define CBMOE_NOALLOC_SCRATCH_BYTES (24u << 20)
+#define CBMOE_NOALLOC_SCRATCH_BYTES (48u << 20)
 int cbmoe_experts_apply_noalloc(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx,
                                 const float* w, int k, float limit, float* y, cudaStream_t stream);
 

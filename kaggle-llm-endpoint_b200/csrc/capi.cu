@@ -35,37 +35,47 @@ int decode_nt_routed(int N, int k, int E) {
 }
 
 // Workspace of the decode path:
-//   plan | h (Rp x 2I bf16) | y_sorted (Rp x H f32) | h_shared (N x 2I bf16) |
-//   scheduling words: routed [gate/up next, down next, gate/up split counters...] (zeroed by the plan kernel),
-//                     shared [gate/up next, down next, split counters...] (zeroed by a memset on the side stream) |
-//   split-K partial sums of the routed gate/up, the shared gate/up and the shared down.
+//   plan | h (Rp x 2I bf16) | y_sorted (Rp x H f32) | h_shared (N x 2I bf16) | y_shared (N x H f32) |
+//   scheduling words: routed [gate/up tickets, down tickets, gate/up item counters, down item counters]
+//                     (zeroed by the plan kernel), shared [the same] (zeroed by a memset on the side stream) |
+//   partial sums of the tail items' pieces of the routed gate/up, routed down, shared gate/up, shared down.
+
+// Tail items a decode launch cuts into pieces: at most half its resident grid (the kernel takes the same bound).
+int decode_tail_items(long long items) {
+  const long long half = (long long)num_sms() * kDecodeMaxCtasPerSm / 2;
+  return (int)(items < half ? items : half);
+}
 
 DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k) {
   DecodeWorkspace w;
   w.nt = decode_nt_routed(N, k, E);
+  w.nt_s = decode_nt(N);
   const int pt = 8 * w.nt;
   w.L = host_plan_layout(N, k, E, 1, pt);
   w.Rp = (int)(w.L.off[8] - w.L.off[7]);
   w.P = (int)(w.L.off[11] - w.L.off[10]);
-  w.Ps = (N + 8 * decode_nt(N) - 1) / (8 * decode_nt(N));   // shared-expert passes
+  w.Ps = (N + 8 * w.nt_s - 1) / (8 * w.nt_s);   // shared-expert passes
   w.RB_gu = I / kRowsPerBlock;
   w.RB_dn = H / kRowsPerBlock;
-  const int KS_gu = H / kStageK, KS_dn = I / kStageK;
-  // K splits: small batches have few (expert, row block) items; splitting K evens out the SMs' share of work
-  w.kq_gu = N <= 16 ? (KS_gu < 4 ? KS_gu : 4) : 1;
-  w.kq_sgu = N <= 16 ? (KS_gu < 5 ? KS_gu : 5) : 1;
-  w.kq_sdn = 1;   // measured: the last-arriver reduction costs more than it balances on this 80-block kernel
-  w.n_zero_routed = 2 + w.P * w.RB_gu;
-  w.n_zero_shared = 2 + w.Ps * w.RB_gu + w.Ps * w.RB_dn;
+  w.tail_gu = decode_tail_items((long long)w.P * w.RB_gu);
+  w.tail_dn = decode_tail_items((long long)w.P * w.RB_dn);
+  w.tail_sgu = decode_tail_items((long long)w.Ps * w.RB_gu);
+  w.tail_sdn = decode_tail_items((long long)w.Ps * w.RB_dn);
+  if (w.tail_sgu > kSideCtas / 2) w.tail_sgu = kSideCtas / 2;
+  if (w.tail_sdn > kSideCtas / 2) w.tail_sdn = kSideCtas / 2;
+  w.n_zero_routed = 2 + w.P * (w.RB_gu + w.RB_dn);
+  w.n_zero_shared = 2 + w.Ps * (w.RB_gu + w.RB_dn);
   w.plan = 0;
   w.h = align_up((size_t)w.L.off[13] * 4);
   w.y = w.h + align_up((size_t)w.Rp * 2 * I * 2);
   w.hs = w.y + align_up((size_t)w.Rp * H * 4);
-  w.sched = w.hs + align_up((size_t)N * 2 * I * 2);
-  w.part_gu = w.sched + align_up((size_t)(w.n_zero_routed + w.n_zero_shared) * 4);
-  w.part_sgu = w.part_gu + (w.kq_gu > 1 ? align_up((size_t)w.kq_gu * w.Rp * 2 * I * 4) : 0);
-  w.part_sdn = w.part_sgu + (w.kq_sgu > 1 ? align_up((size_t)w.kq_sgu * N * 2 * I * 4) : 0);
-  w.total = w.part_sdn + (w.kq_sdn > 1 ? align_up((size_t)w.kq_sdn * N * H * 4) : 0);
+  w.ys = w.hs + align_up((size_t)N * 2 * I * 2);
+  w.done = w.ys + align_up((size_t)N * H * 4);
+  w.part_gu = w.done + align_up((size_t)(w.n_zero_routed + w.n_zero_shared) * 4);
+  w.part_dn = w.part_gu + align_up(decode_part_bytes(w.tail_gu, w.nt, 2));
+  w.part_sgu = w.part_dn + align_up(decode_part_bytes(w.tail_dn, w.nt, 1));
+  w.part_sdn = w.part_sgu + align_up(decode_part_bytes(w.tail_sgu, w.nt_s, 2));
+  w.total = w.part_sdn + align_up(decode_part_bytes(w.tail_sdn, w.nt_s, 1));
   return w;
 }
 
@@ -86,8 +96,6 @@ bool shared_ok(const cbmoe_shared* sh) {
 DecodeParams base_params() {
   DecodeParams p{};
   p.E = 1;
-  p.topk = 1;
-  p.KQ = 1;
   return p;
 }
 
@@ -114,8 +122,8 @@ int side_stream(SideStream** out) {
 int routed_decode(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx, const float* w, int k,
                   float limit, uint8_t* ws, const DecodeWorkspace& W, cudaStream_t stream) {
   int32_t* plan = reinterpret_cast<int32_t*>(ws + W.plan);
-  int* sched = reinterpret_cast<int*>(ws + W.sched);
-  int rc = launch_route_plan(idx, w, N, k, ex->E, 1, 8 * W.nt, plan, stream, sched, W.n_zero_routed);
+  int* done = reinterpret_cast<int*>(ws + W.done);
+  int rc = launch_route_plan(idx, w, N, k, ex->E, 1, 8 * W.nt, plan, stream, done, W.n_zero_routed);
   if (rc) return rc;
   uint16_t* h = reinterpret_cast<uint16_t*>(ws + W.h);
   float* ys = reinterpret_cast<float*>(ws + W.y);
@@ -138,11 +146,10 @@ int routed_decode(const cbmoe_experts* ex, const uint16_t* x, int N, const int32
   p.E = ex->E;
   p.limit = limit;
   p.h_out = h;
-  p.KQ = W.kq_gu;
-  p.sched = sched;
-  p.done = sched + 2;
+  p.sched = done;
+  p.tail_items = W.tail_gu;
+  p.done = done + 2;
   p.part = reinterpret_cast<float*>(ws + W.part_gu);
-  p.part_rows = W.Rp;
   rc = decode_cb3_gateup(p, W.nt, stream);
   if (rc) return rc;
 
@@ -158,11 +165,63 @@ int routed_decode(const cbmoe_experts* ex, const uint16_t* x, int N, const int32
   d.tok_row = nullptr;
   d.h_out = nullptr;
   d.y_out = ys;
-  d.KQ = 1;
-  d.sched = sched + 1;
-  d.done = nullptr;
-  d.part = nullptr;
+  d.sched = done + 1;
+  d.tail_items = W.tail_dn;
+  d.done = done + 2 + W.P * W.RB_gu;
+  d.part = reinterpret_cast<float*>(ws + W.part_dn);
   return decode_cb3_down(d, W.nt, stream);
+}
+
+int shared_side(const cbmoe_shared* sh, const uint16_t* x, int N, int H, int I, float limit, uint8_t* ws,
+                const DecodeWorkspace& W, SideStream* side, cudaStream_t stream) {
+  CBMOE_CUDA_TRY(cudaEventRecord(side->fork, stream));
+  CBMOE_CUDA_TRY(cudaStreamWaitEvent(side->s, side->fork, 0));
+  int* done_sh = reinterpret_cast<int*>(ws + W.done) + W.n_zero_routed;
+  CBMOE_CUDA_TRY(cudaMemsetAsync(done_sh, 0, (size_t)W.n_zero_shared * 4, side->s));
+  uint16_t* hs = reinterpret_cast<uint16_t*>(ws + W.hs);
+
+  DecodeParams p = base_params();
+  p.wq = static_cast<const uint8_t*>(sh->gateup_q);
+  p.s0 = sh->gate_s;
+  p.s1 = sh->up_s;
+  p.scale_axis = sh->scale_axis;
+  p.rows = I;
+  p.K = H;
+  p.RB = I / kRowsPerBlock;
+  p.KS = H / kStageK;
+  p.b = x;
+  p.N = N;
+  p.limit = limit;
+  p.h_out = hs;
+  p.grid_cap = kSideCtas;
+  p.sched = done_sh;
+  p.tail_items = W.tail_sgu;
+  p.done = done_sh + 2;
+  p.part = reinterpret_cast<float*>(ws + W.part_sgu);
+  int rc = decode_w8_gateup(p, W.nt_s, side->s);
+  if (rc) return rc;
+
+  DecodeParams d = base_params();
+  d.wq = static_cast<const uint8_t*>(sh->down_q);
+  d.s0 = sh->down_s;
+  d.scale_axis = sh->scale_axis;
+  d.rows = H;
+  d.K = I;
+  d.RB = H / kRowsPerBlock;
+  d.KS = I / kStageK;
+  d.b = hs;
+  d.b_hilo = 1;
+  d.N = N;
+  d.y_out = reinterpret_cast<float*>(ws + W.ys);
+  d.grid_cap = kSideCtas;
+  d.sched = done_sh + 1;
+  d.tail_items = W.tail_sdn;
+  d.done = done_sh + 2 + W.Ps * W.RB_gu;
+  d.part = reinterpret_cast<float*>(ws + W.part_sdn);
+  rc = decode_w8_down_store(d, W.nt_s, side->s);
+  if (rc) return rc;
+  CBMOE_CUDA_TRY(cudaEventRecord(side->join, side->s));
+  return CBMOE_OK;
 }
 
 // Slots (N*k) above which CBMOE_PATH_AUTO takes the grouped tensor-core path.
@@ -300,7 +359,7 @@ extern "C" int cbmoe_experts_apply(const cbmoe_experts* ex, const uint16_t* x, i
                                    size_t workspace_bytes, cudaStream_t stream) {
   int rc = check_common(ex, x, N, idx, w, k, path);
   if (rc) return rc;
-  if (N > 0 && !y) return CBMOE_ERR_INVALID;
+  if (N > 0 && (!y || !aligned16(y))) return CBMOE_ERR_INVALID;
   if (N == 0) return CBMOE_OK;
   if (pick_path(N, k, path) == CBMOE_PATH_GROUPED) {
     const GroupedWorkspace G = grouped_workspace(ex->E, ex->H, ex->I, N, k);
@@ -318,7 +377,8 @@ extern "C" int cbmoe_experts_apply(const cbmoe_experts* ex, const uint16_t* x, i
   rc = routed_decode(ex, x, N, idx, w, k, limit, ws, W, stream);
   if (rc) return rc;
   const int32_t* plan = reinterpret_cast<const int32_t*>(ws + W.plan);
-  return launch_combine(reinterpret_cast<const float*>(ws + W.y), plan + W.L.off[9], w, N, k, ex->H, y, stream);
+  return launch_combine(reinterpret_cast<const float*>(ws + W.y), plan + W.L.off[9], w, N, k, ex->H, nullptr, y,
+                        nullptr, stream);
 }
 
 extern "C" int cbmoe_moe_layer(const cbmoe_experts* ex, const cbmoe_shared* sh, const uint16_t* x, int N,
@@ -326,7 +386,7 @@ extern "C" int cbmoe_moe_layer(const cbmoe_experts* ex, const cbmoe_shared* sh, 
                                void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   int rc = check_common(ex, x, N, idx, w, k, path);
   if (rc) return rc;
-  if (!shared_ok(sh) || (N > 0 && !out)) return CBMOE_ERR_INVALID;
+  if (!shared_ok(sh) || (N > 0 && (!out || !aligned16(out)))) return CBMOE_ERR_INVALID;
   if (N == 0) return CBMOE_OK;
   if (pick_path(N, k, path) == CBMOE_PATH_GROUPED) {
     const GroupedWorkspace G = grouped_workspace(ex->E, ex->H, ex->I, N, k);
@@ -365,64 +425,17 @@ extern "C" int cbmoe_moe_layer(const cbmoe_experts* ex, const cbmoe_shared* sh, 
   const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k);
   if (!workspace || workspace_bytes < W.total) return CBMOE_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  uint16_t* hs = reinterpret_cast<uint16_t*>(ws + W.hs);
   SideStream* side = nullptr;
   rc = side_stream(&side);
   if (rc) return rc;
-  CBMOE_CUDA_TRY(cudaEventRecord(side->fork, stream));
-  CBMOE_CUDA_TRY(cudaStreamWaitEvent(side->s, side->fork, 0));
-  int* sched_sh = reinterpret_cast<int*>(ws + W.sched) + W.n_zero_routed;
-  CBMOE_CUDA_TRY(cudaMemsetAsync(sched_sh, 0, (size_t)W.n_zero_shared * 4, side->s));
-
-  DecodeParams p = base_params();
-  p.wq = static_cast<const uint8_t*>(sh->gateup_q);
-  p.s0 = sh->gate_s;
-  p.s1 = sh->up_s;
-  p.scale_axis = sh->scale_axis;
-  p.rows = ex->I;
-  p.K = ex->H;
-  p.RB = ex->I / kRowsPerBlock;
-  p.KS = ex->H / kStageK;
-  p.b = x;
-  p.N = N;
-  p.limit = limit;
-  p.h_out = hs;
-  p.KQ = W.kq_sgu;
-  p.sched = sched_sh;
-  p.done = sched_sh + 2;
-  p.part = reinterpret_cast<float*>(ws + W.part_sgu);
-  p.part_rows = N;
-  rc = decode_w8_gateup(p, decode_nt(N), side->s);
+  rc = shared_side(sh, x, N, ex->H, ex->I, limit, ws, W, side, stream);
   if (rc) return rc;
-  CBMOE_CUDA_TRY(cudaEventRecord(side->join, side->s));
-
   rc = routed_decode(ex, x, N, idx, w, k, limit, ws, W, stream);
   CBMOE_CUDA_TRY(cudaStreamWaitEvent(stream, side->join, 0));   // join even when a routed launch failed
   if (rc) return rc;
   const int32_t* plan = reinterpret_cast<const int32_t*>(ws + W.plan);
-
-  DecodeParams d = base_params();
-  d.wq = static_cast<const uint8_t*>(sh->down_q);
-  d.s0 = sh->down_s;
-  d.scale_axis = sh->scale_axis;
-  d.rows = ex->H;
-  d.K = ex->I;
-  d.RB = ex->H / kRowsPerBlock;
-  d.KS = ex->I / kStageK;
-  d.b = hs;
-  d.b_hilo = 1;
-  d.N = N;
-  d.y_sorted = reinterpret_cast<const float*>(ws + W.y);
-  d.row_slot = plan + W.L.off[9];
-  d.wts = w;
-  d.topk = k;
-  d.out_bf16 = out;
-  d.KQ = W.kq_sdn;
-  d.sched = sched_sh + 1;
-  d.done = sched_sh + 2 + W.Ps * W.RB_gu;
-  d.part = reinterpret_cast<float*>(ws + W.part_sdn);
-  d.part_rows = N;
-  return decode_w8_down_combine(d, decode_nt(N), stream);
+  return launch_combine(reinterpret_cast<const float*>(ws + W.y), plan + W.L.off[9], w, N, k, ex->H,
+                        reinterpret_cast<const float*>(ws + W.ys), nullptr, out, stream);
 }
 
 extern "C" size_t cbmoe_matvec_workspace_bytes(int N) { return N >= 0 ? 0 : 0; }
@@ -490,7 +503,7 @@ extern "C" int cbmoe_w8_linear(const void* qk, const float* s, int scale_axis, i
 // owns, a plugin host that forbids allocation inside its execute callback, or host code that must not block on
 // cudaMalloc (which can synchronize the device). This entry point keeps its scratch in a file-scope device array
 // instead. The array is part of the library image: every GPU that loads the library holds
-// kNoAllocScratchBytes (24 MiB) of device memory for it until the process exits, whether or not this entry point
+// kNoAllocScratchBytes (48 MiB) of device memory for it until the process exits, whether or not this entry point
 // is ever called. Requests that need more scratch than that are rejected with CBMOE_ERR_WORKSPACE.
 //
 // In host code the name `g_noalloc_scratch` is only a host-side stand-in for the device array, not its device
@@ -511,7 +524,7 @@ extern "C" int cbmoe_experts_apply_noalloc(const cbmoe_experts* ex, const uint16
                                            const float* w, int k, float limit, float* y, cudaStream_t stream) {
   int rc = check_common(ex, x, N, idx, w, k, CBMOE_PATH_DECODE);
   if (rc) return rc;
-  if (N > 0 && !y) return CBMOE_ERR_INVALID;
+  if (N > 0 && (!y || !aligned16(y))) return CBMOE_ERR_INVALID;
   if (N == 0) return CBMOE_OK;
   const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k);
   if (W.total > kNoAllocScratchBytes) return CBMOE_ERR_WORKSPACE;   // request needs more than the fixed array
@@ -532,5 +545,6 @@ extern "C" int cbmoe_experts_apply_noalloc(const cbmoe_experts* ex, const uint16
   rc = routed_decode(ex, x, N, idx, w, k, limit, ws, W, stream);
   if (rc) return rc;
   const int32_t* plan = reinterpret_cast<const int32_t*>(ws + W.plan);
-  return launch_combine(reinterpret_cast<const float*>(ws + W.y), plan + W.L.off[9], w, N, k, ex->H, y, stream);
+  return launch_combine(reinterpret_cast<const float*>(ws + W.y), plan + W.L.off[9], w, N, k, ex->H, nullptr, y,
+                        nullptr, stream);
 }

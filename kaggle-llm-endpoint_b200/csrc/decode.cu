@@ -8,9 +8,9 @@
 //     into shared memory with bulk async copies (mbarrier pipeline, NSTAGE deep); four consumer warps turn them
 //     into bf16 tensor-core fragments with byte permutes (CB3K) or int8 -> fp32 * scale -> bf16 (W8K) and
 //     multiply them with mma.sync m16n8k16 against the pass's tokens, accumulating in fp32.
-// Persistent grid: gridDim = SMs x resident CTAs; CTA b takes items b, b + gridDim, ... of (pass, row block).
+// Persistent grid: gridDim = SMs x resident CTAs, each streaming an equal share of all items' stages (stream-K).
 // Epilogues: SWIGLU (gate+up -> h stored as bf16 hi + bf16 lo, so the down matvec sees h to ~16 mantissa bits),
-// STORE (fp32 rows), COMBINE (shared-expert down + the routed slots' weighted sum -> bf16 layer output).
+// STORE (fp32 rows). The layer's weighted sum of the slots (+ the shared expert) is combine_kernel.
 #include "decode.cuh"
 #include "profile.cuh"
 
@@ -43,7 +43,50 @@ __device__ __forceinline__ PassInfo get_pass(const DecodeParams& p, int pass, in
 
 __device__ __forceinline__ int count_items(const DecodeParams& p, int pass_tokens) {
   const int np = (p.pass_expert == nullptr) ? (p.N + pass_tokens - 1) / pass_tokens : *p.n_pass;
-  return np * p.RB * p.KQ;
+  return np * p.RB;
+}
+
+// Work distribution. An item is (pass, 64-row block): KS stages of weights for the pass's tokens. CTAs take work
+// from a shared ticket counter, so the CTAs that start late (their SM still busy with another kernel) or run slow
+// simply take less. Tickets first hand out whole items; the last n_tail items are cut into Q pieces of ~KS/Q stages
+// each, so the grid runs out of work within a fraction of an item. A piece stores its partial sums in the item's
+// slot q; the piece that arrives last on the item's counter adds the Q slots up in order (deterministic) and runs
+// the epilogue. Without partial-sum space (part == nullptr) every item is whole.
+struct Schedule {
+  int n_items, n_whole, n_tail, Q, KS;
+  __device__ int tickets() const { return n_whole + n_tail * Q; }
+  // ticket -> item, stage range, piece (-1: whole item)
+  __device__ void decode(int t, int& item, int& ks0, int& ks1, int& piece) const {
+    if (t < n_whole) {
+      item = t;
+      ks0 = 0;
+      ks1 = KS;
+      piece = -1;
+      return;
+    }
+    const int u = t - n_whole;
+    item = n_whole + u / Q;
+    piece = u % Q;
+    ks0 = piece * KS / Q;
+    ks1 = (piece + 1) * KS / Q;
+  }
+};
+
+__device__ __forceinline__ Schedule make_schedule(const DecodeParams& p, int n_items) {
+  Schedule sc;
+  sc.n_items = n_items;
+  sc.KS = p.KS;
+  sc.Q = p.KS < kDecodePieces ? p.KS : kDecodePieces;
+  int tail = 0;
+  if (p.part != nullptr && p.done != nullptr && sc.Q > 1) {
+    tail = (int)gridDim.x / 2 > 1 ? (int)gridDim.x / 2 : 1;
+    if (tail > p.tail_items) tail = p.tail_items;
+    if (tail > n_items) tail = n_items;
+  }
+  sc.n_tail = tail;
+  sc.n_whole = n_items - tail;
+  if (tail == 0) sc.Q = 1;
+  return sc;
 }
 
 // Auxiliary bytes the producer copies into a stage: the item's codebooks (CB3K) or row scales (W8K
@@ -58,39 +101,25 @@ __device__ __forceinline__ int aux_bytes(const DecodeParams& p, bool first) {
 // arrive, which releases it). item < 0 ends the consumers' loop.
 struct StageHdr {
   int item, e, row0, cnt;
-  int rb, kq, ks, flags;  // flags: 1 = first stage of the item, 2 = last stage of the item
+  int rb, kq, ks, flags;  // kq: the segment's partial-sum slot; flags: 1 = first stage of the segment,
+                          // 2 = last stage of the segment, bits 8+: segments of the item (1 = whole)
 };
 
 __device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32)); }
 
-// Sum over token `row`'s routed slots of w * y_sorted[slot row][r]. The slot rows and weights are loaded first and
-// the (up to 16 at a time) y loads issued together, so the epilogue waits for two memory round trips, not 2k.
-__device__ __forceinline__ float routed_sum(const DecodeParams& p, int row, int r) {
-  float v = 0.f;
-  for (int q0 = 0; q0 < p.topk; q0 += 16) {
-    int rs[16];
-    float wt[16], y[16];
-#pragma unroll
-    for (int q = 0; q < 16; ++q) {
-      const bool in = q0 + q < p.topk;
-      rs[q] = in ? p.row_slot[row * p.topk + q0 + q] : -1;
-      wt[q] = in ? p.wts[row * p.topk + q0 + q] : 0.f;
-    }
-#pragma unroll
-    for (int q = 0; q < 16; ++q) y[q] = rs[q] >= 0 ? p.y_sorted[(size_t)rs[q] * p.rows + r] : 0.f;
-#pragma unroll
-    for (int q = 0; q < 16; ++q) v += wt[q] * y[q];
-  }
-  return v;
-}
-
 // The kernel proper; HILO is a template argument so the B staging size is a compile-time constant.
-//   producer warp: takes items (pass, 64-row block, K split) from the next-item counter (or round-robin), and for
-//                  each of the item's 256-input stages fills a ring slot: header, weights, aux, the pass's B rows;
-//   consumer warps: dequantize + MMA per stage, then the item's epilogue; with K splits, each split stores its
-//                  partial sums and the last split to arrive adds them up and runs the epilogue.
+//   producer warp: walks the CTA's stage range item by item (pass, 64-row block) and for each 256-input stage
+//                  fills a ring slot: header, weights, aux, the pass's B rows;
+//   consumer warps: dequantize + MMA per stage, then the segment's epilogue (whole item) or partial sums (cut
+//                  item, finished by its last-arriving segment).
+#ifndef CBMOE_DECODE_MINB_NT1
+#define CBMOE_DECODE_MINB_NT1 1
+#endif
+template <int NT>
+constexpr int decode_min_blocks() { return NT == 1 ? CBMOE_DECODE_MINB_NT1 : 1; }
+
 template <int FMT, int NMAT, int NT, int EPI, int HILO, int NSTAGE>
-__global__ void __launch_bounds__(kDecodeThreads) decode_kernel_t(const DecodeParams p) {
+__global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<NT>()) decode_kernel_t(const DecodeParams p) {
   using SM = DecodeSmem<FMT, NMAT, NT, HILO, NSTAGE>;
   constexpr int kPassTokens = NT * 8;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -111,76 +140,124 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel_t(const DecodePa
   __syncthreads();
 
   const int n_items = count_items(p, kPassTokens);
-  const int RB = p.RB, KS = p.KS, KQ = p.KQ;
+  const int RB = p.RB, KS = p.KS;
+  const Schedule sc = make_schedule(p, n_items);
+  const int n_tickets = sc.tickets();
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------------------------------------ producer
+    // Items are taken one ahead: the next item's number (a ticket from the shared counter) and its pass record
+    // (expert, first row, count) are requested before the current item's stages are issued, and the next item's
+    // B rows right after its first stage, so their global-memory round trips overlap the current item's copies.
     int st = 0;
     uint32_t ph = 0;
     int iter = 0;
-    for (;;) {
-      int item = 0;
-      if (lane == 0) item = p.sched ? atomicAdd(p.sched, 1) : (int)blockIdx.x + iter * (int)gridDim.x;
-      item = __shfl_sync(0xffffffffu, item, 0);
+    auto take = [&]() -> int {   // meaningful in lane 0 only
+      int tk = 0;
+      if (lane == 0) tk = p.sched ? atomicAdd(p.sched, 1) : (int)blockIdx.x + iter * (int)gridDim.x;
       ++iter;
-      if (item >= n_items) {
-        bool ok = true;
-        if (lane == 0) {
-          ok = mbar_wait_sleepy(&empty[st], ph ^ 1);
-          if (ok) {
-            hdr[st].item = -1;
-            mbar_arrive(&full[st]);
-          }
-        }
-        return;
-      }
-      const int kq = item % KQ, rest = item / KQ;
-      const int rb = rest % RB, pass = rest / RB;
-      const PassInfo pi = get_pass(p, pass, kPassTokens);
-      if (pi.e < 0 || pi.e >= p.E || pi.cnt <= 0) continue;
-      int brow = -1;
-      if (lane < pi.cnt) brow = p.tok_row ? p.tok_row[pi.row0 + lane] : pi.row0 + lane;
-      const int n_copies = __popc(__ballot_sync(0xffffffffu, brow >= 0));
-      const int ks0 = kq * KS / KQ, ks1 = (kq + 1) * KS / KQ;
-      for (int ks = ks0; ks < ks1; ++ks) {
-        const bool first = ks == ks0;
-        const int aux = aux_bytes<FMT, NMAT>(p, first);
-        bool ok = true;
-        if (lane == 0) {
-          ok = mbar_wait_sleepy(&empty[st], ph ^ 1);
-          if (ok) {
-            hdr[st] = {item, pi.e, pi.row0, pi.cnt, rb, kq, ks, (first ? 1 : 0) | (ks == ks1 - 1 ? 2 : 0)};
-            mbar_arrive_expect_tx(&full[st], SM::kWBytes + aux + n_copies * SM::kBCopy);
-          }
-        }
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (!ok) return;
-        uint8_t* sw = stages + st * SM::kStage;
-        uint8_t* sa = sw + SM::kWBytes;
-        if (lane == 0) {
-          const uint8_t* src = p.wq + unit_offset(pi.e, rb, ks, 0, 0, RB, KS, NMAT, SM::kUnit);
-          bulk_g2s(sw, src, SM::kWBytes, &full[st]);
-        }
-        if (aux > 0 && lane < NMAT) {
-          if constexpr (FMT == kFmtCB3) {
-            if (lane == 0) bulk_g2s(sa, p.cb + cb_offset_words(pi.e, rb, 0, 0, 0, RB, NMAT), aux, &full[st]);
-          } else {
-            const float* sc = (lane == 0) ? p.s0 : p.s1;
-            const int per = aux / NMAT;
-            const float* src = (p.scale_axis == 1) ? sc + rb * kRowsPerBlock : sc + ks * kStageK;
-            bulk_g2s(sa + lane * per, src, per, &full[st]);
-          }
-        }
-        if (brow >= 0) {
-          const uint16_t* src = p.b + (size_t)brow * (p.K * (HILO ? 2 : 1)) + (size_t)ks * kStageK * (HILO ? 2 : 1);
-          bulk_g2s(sw + SM::kWBytes + SM::kAuxBytes + lane * SM::kBRow, src, SM::kBCopy, &full[st]);
-        }
-        if (++st == NSTAGE) {
-          st = 0;
-          ph ^= 1;
-        }
-      }
+      return tk;
+    };
+    auto pass_of = [&](int it) -> PassInfo { return get_pass(p, it / RB, kPassTokens); };
+    auto b_row = [&](const PassInfo& q) -> int {
+      if (lane >= q.cnt || q.cnt <= 0) return -1;
+      return p.tok_row ? p.tok_row[q.row0 + lane] : q.row0 + lane;
+    };
+    // The next ticket is taken kLookahead stages before the current one's last stage is issued, its pass record
+    // read one stage later and its B rows one more, so their round trips overlap the copies; taking it later than
+    // that would stall the ring, earlier would commit this CTA to more work while others may run dry.
+    constexpr int kLookahead = 3;
+    int tk = __shfl_sync(0xffffffffu, take(), 0);
+    int item = 0, ks0 = 0, ks1 = 0, piece = -1;
+    PassInfo pi{-1, 0, 0};
+    int brow = -1;
+    if (tk < n_tickets) {
+      sc.decode(tk, item, ks0, ks1, piece);
+      pi = pass_of(item);
+      brow = b_row(pi);
     }
+    while (tk < n_tickets) {
+      int pending = 0, tn = 0;
+      int item_n = 0, ks0_n = 0, ks1_n = 0, piece_n = -1;
+      PassInfo pn{-1, 0, 0};
+      bool has_n = false;
+      int brow_n = -1;
+      int next_step = 0;   // 0: take the ticket, 1: read its pass record, 2: its B rows, 3: done
+      auto advance = [&]() {
+        if (next_step == 0) {
+          pending = take();
+        } else if (next_step == 1) {
+          tn = __shfl_sync(0xffffffffu, pending, 0);
+          has_n = tn < n_tickets;
+          if (has_n) {
+            sc.decode(tn, item_n, ks0_n, ks1_n, piece_n);
+            pn = pass_of(item_n);
+          }
+        } else if (next_step == 2) {
+          if (has_n) brow_n = b_row(pn);
+        }
+        ++next_step;
+      };
+      const int rb = item % RB;
+      const int nseg = piece < 0 ? 1 : sc.Q;
+      if (pi.e >= 0 && pi.e < p.E && pi.cnt > 0) {
+        const int n_copies = __popc(__ballot_sync(0xffffffffu, brow >= 0));
+        for (int ks = ks0; ks < ks1; ++ks) {
+          const bool first = ks == ks0;
+          const int aux = aux_bytes<FMT, NMAT>(p, first);
+          bool ok = true;
+          if (lane == 0) {
+            ok = mbar_wait_sleepy(&empty[st], ph ^ 1);
+            if (ok) {
+              hdr[st] = {item, pi.e, pi.row0, pi.cnt, rb, piece < 0 ? 0 : piece, ks,
+                         (first ? 1 : 0) | (ks == ks1 - 1 ? 2 : 0) | (nseg << 8)};
+              mbar_arrive_expect_tx(&full[st], SM::kWBytes + aux + n_copies * SM::kBCopy);
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          if (!ok) return;
+          uint8_t* sw = stages + st * SM::kStage;
+          uint8_t* sa = sw + SM::kWBytes;
+          if (lane == 0) {
+            const uint8_t* src = p.wq + unit_offset(pi.e, rb, ks, 0, 0, RB, KS, NMAT, SM::kUnit);
+            bulk_g2s(sw, src, SM::kWBytes, &full[st]);
+          }
+          if (aux > 0 && lane < NMAT) {
+            if constexpr (FMT == kFmtCB3) {
+              if (lane == 0) bulk_g2s(sa, p.cb + cb_offset_words(pi.e, rb, 0, 0, 0, RB, NMAT), aux, &full[st]);
+            } else {
+              const float* scl = (lane == 0) ? p.s0 : p.s1;
+              const int per = aux / NMAT;
+              const float* src = (p.scale_axis == 1) ? scl + rb * kRowsPerBlock : scl + ks * kStageK;
+              bulk_g2s(sa + lane * per, src, per, &full[st]);
+            }
+          }
+          if (brow >= 0) {
+            const uint16_t* src =
+                p.b + (size_t)brow * (p.K * (HILO ? 2 : 1)) + (size_t)ks * kStageK * (HILO ? 2 : 1);
+            bulk_g2s(sw + SM::kWBytes + SM::kAuxBytes + lane * SM::kBRow, src, SM::kBCopy, &full[st]);
+          }
+          if (++st == NSTAGE) {
+            st = 0;
+            ph ^= 1;
+          }
+          if (ks >= ks1 - kLookahead && next_step < 3) advance();
+        }
+      }
+      while (next_step < 3) advance();
+      tk = tn;
+      item = item_n;
+      ks0 = ks0_n;
+      ks1 = ks1_n;
+      piece = piece_n;
+      pi = pn;
+      brow = brow_n;
+    }
+    if (lane == 0 && mbar_wait_sleepy(&empty[st], ph ^ 1)) {
+      hdr[st].item = -1;
+      mbar_arrive(&full[st]);
+    }
+    return;
   }
 
   // -------------------------------------------------------------------------------------------- consumers
@@ -189,11 +266,88 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel_t(const DecodePa
   uint32_t ph = 0;
   Codebook cbg[NMAT], cbh[NMAT];
   float sg[NMAT], sh[NMAT];
+  // Few accumulator tiles per warp (NT * NMAT <= 2) make a long chain of dependent MMAs per stage; a second set
+  // (odd MMA steps, or the h-lo products with HILO) halves it and is added in before the epilogue.
+  constexpr int kAccSets = (NT * NMAT <= 2) ? 2 : 1;
   float acc[NMAT][NT][4];
+  float acc_b[kAccSets > 1 ? NMAT : 1][NT][4];
+
+  // Epilogue of one item from acc (the item's full sums).
+  auto epilogue = [&](const StageHdr& e) {
+    const int rowbase = e.rb * kRowsPerBlock + warp * kRowsPerWarp;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int j = n * 8 + 2 * t + (i & 1);
+        const int r = rowbase + g + ((i & 2) ? 8 : 0);
+        if (j >= e.cnt) continue;
+        const int row = e.row0 + j;
+        if constexpr (EPI == kEpiSwiglu) {
+          const float hv = swiglu_clamped(acc[0][n][i], acc[NMAT - 1][n][i], p.limit);
+          const __nv_bfloat16 hi = __float2bfloat16_rn(hv);
+          const __nv_bfloat16 lo = __float2bfloat16_rn(hv - __bfloat162float(hi));
+          uint16_t* dst = p.h_out + (size_t)row * (2 * p.rows) + (r / kStageK) * (2 * kStageK) + (r % kStageK);
+          dst[0] = *reinterpret_cast<const uint16_t*>(&hi);
+          dst[kStageK] = *reinterpret_cast<const uint16_t*>(&lo);
+        } else {
+          p.y_out[(size_t)row * p.rows + r] = acc[0][n][i];
+        }
+      }
+    }
+  };
+  // Tail items cut into pieces (Schedule, above): a piece's partial sums go to the item's slot q when it ends;
+  // its arrival on the item's counter (fence + atomic) is counted after the next stage, and the atomic's result is
+  // read when the next piece or item ends (or when the consumers stop), so no global round trip stalls the MMAs.
+  // The last arriver adds the Q slots up and runs the epilogue.
+  constexpr int kSlotFloats = kPassTokens * NMAT * kRowsPerBlock;
+  int pend_state = 0;   // 0: nothing pending, 1: partials stored, 2: arrival counted (ticket in thread 0)
+  StageHdr pend{};
+  int ticket = 0;
+  auto slot_at = [&](int item, int q, int j, int m, int rl) -> size_t {
+    return ((size_t)(item - sc.n_whole) * sc.Q + q) * kSlotFloats + ((size_t)j * NMAT + m) * kRowsPerBlock + rl;
+  };
+  auto count_arrival = [&]() {
+    __threadfence();
+    consumer_bar();
+    if (threadIdx.x == 0) ticket = atomicAdd(&p.done[pend.item], 1);
+    pend_state = 2;
+  };
+  auto resolve = [&]() {
+    const int nseg = pend.flags >> 8;
+    if (threadIdx.x == 0) {
+      s_flag = (ticket == nseg - 1) ? 1 : 0;
+      if (s_flag) p.done[pend.item] = 0;   // every segment has arrived: ready for the next launch
+    }
+    consumer_bar();
+    pend_state = 0;
+    if (!s_flag) return;
+    __threadfence();
+    const int rl0 = warp * kRowsPerWarp + g;
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int j = n * 8 + 2 * t + (i & 1);
+          const int rl = rl0 + ((i & 2) ? 8 : 0);
+          float v = 0.f;
+          if (j < pend.cnt)
+            for (int q = 0; q < nseg; ++q) v += __ldcg(&p.part[slot_at(pend.item, q, j, m, rl)]);
+          acc[m][n][i] = v;
+        }
+    epilogue(pend);
+  };
+
   for (;;) {
     if (!mbar_wait(&full[st], ph)) return;
     const StageHdr h = hdr[st];
-    if (h.item < 0) return;
+    if (h.item < 0) {
+      if (pend_state == 1) count_arrival();
+      if (pend_state == 2) resolve();
+      return;
+    }
     const uint8_t* sw = stages + st * SM::kStage;
     const uint8_t* sa = sw + SM::kWBytes;
     const uint8_t* sb = sa + SM::kAuxBytes;
@@ -216,7 +370,10 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel_t(const DecodePa
 #pragma unroll
         for (int n = 0; n < NT; ++n)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) acc[m][n][i] = 0.f;
+          for (int i = 0; i < 4; ++i) {
+            acc[m][n][i] = 0.f;
+            if constexpr (kAccSets > 1) acc_b[m][n][i] = 0.f;
+          }
       }
     }
 
@@ -272,8 +429,17 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel_t(const DecodePa
 #pragma unroll
           for (int n = 0; n < NT; ++n) {
             if (n == 0 || n * 8 < h.cnt) {
-              mma_bf16(acc[m][n], a[s], bf[n][2 * s], bf[n][2 * s + 1]);
-              if constexpr (HILO) mma_bf16(acc[m][n], a[s], bl[n][2 * s], bl[n][2 * s + 1]);
+              if constexpr (kAccSets > 1) {
+                if constexpr (HILO) {
+                  mma_bf16(acc[m][n], a[s], bf[n][2 * s], bf[n][2 * s + 1]);
+                  mma_bf16(acc_b[m][n], a[s], bl[n][2 * s], bl[n][2 * s + 1]);
+                } else {
+                  mma_bf16((s & 1) ? acc_b[m][n] : acc[m][n], a[s], bf[n][2 * s], bf[n][2 * s + 1]);
+                }
+              } else {
+                mma_bf16(acc[m][n], a[s], bf[n][2 * s], bf[n][2 * s + 1]);
+                if constexpr (HILO) mma_bf16(acc[m][n], a[s], bl[n][2 * s], bl[n][2 * s + 1]);
+              }
             }
           }
         }
@@ -285,12 +451,20 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel_t(const DecodePa
       st = 0;
       ph ^= 1;
     }
+    if (pend_state == 1) count_arrival();
     if (!(h.flags & 2)) continue;
 
     // ---------------------------------------------------------------------------------- item epilogue
-    const int rowbase = h.rb * kRowsPerBlock + warp * kRowsPerWarp;
-    if (KQ > 1) {
-      // store this split's partial sums; the last split to arrive reduces them and runs the epilogue
+    if constexpr (kAccSets > 1) {
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[m][n][i] += acc_b[m][n][i];
+    }
+    if ((h.flags >> 8) > 1) {
+      const int rl0 = warp * kRowsPerWarp + g;
 #pragma unroll
       for (int m = 0; m < NMAT; ++m)
 #pragma unroll
@@ -298,74 +472,33 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel_t(const DecodePa
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int j = n * 8 + 2 * t + (i & 1);
-            const int r = rowbase + g + ((i & 2) ? 8 : 0);
-            if (j < h.cnt)
-              p.part[(((size_t)h.kq * p.part_rows + h.row0 + j) * NMAT + m) * p.rows + r] = acc[m][n][i];
+            if (j < h.cnt) p.part[slot_at(h.item, h.kq, j, m, rl0 + ((i & 2) ? 8 : 0))] = acc[m][n][i];
           }
-      __threadfence();
-      consumer_bar();
-      if (threadIdx.x == 0) {
-        const int slot = (h.item / KQ);
-        s_flag = (atomicAdd(&p.done[slot], 1) == KQ - 1) ? 1 : 0;
-        if (s_flag) p.done[slot] = 0;   // every split has arrived: ready for the next launch
-      }
-      consumer_bar();
-      if (!s_flag) continue;
-      __threadfence();
-#pragma unroll
-      for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int j = n * 8 + 2 * t + (i & 1);
-            const int r = rowbase + g + ((i & 2) ? 8 : 0);
-            float v = 0.f;
-            if (j < h.cnt)
-              for (int q = 0; q < KQ; ++q)
-                v += __ldcg(&p.part[(((size_t)q * p.part_rows + h.row0 + j) * NMAT + m) * p.rows + r]);
-            acc[m][n][i] = v;
-          }
+      if (pend_state == 2) resolve();   // the previous segment's; acc is free again
+      pend = h;
+      pend_state = 1;
+      continue;
     }
-#pragma unroll
-    for (int n = 0; n < NT; ++n) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int j = n * 8 + 2 * t + (i & 1);
-        const int r = rowbase + g + ((i & 2) ? 8 : 0);
-        if (j >= h.cnt) continue;
-        const int row = h.row0 + j;
-        if constexpr (EPI == kEpiSwiglu) {
-          const float hv = swiglu_clamped(acc[0][n][i], acc[NMAT - 1][n][i], p.limit);
-          const __nv_bfloat16 hi = __float2bfloat16_rn(hv);
-          const __nv_bfloat16 lo = __float2bfloat16_rn(hv - __bfloat162float(hi));
-          uint16_t* dst = p.h_out + (size_t)row * (2 * p.rows) + (r / kStageK) * (2 * kStageK) + (r % kStageK);
-          dst[0] = *reinterpret_cast<const uint16_t*>(&hi);
-          dst[kStageK] = *reinterpret_cast<const uint16_t*>(&lo);
-        } else if constexpr (EPI == kEpiStore) {
-          p.y_out[(size_t)row * p.rows + r] = acc[0][n][i];
-        } else {
-          float v = acc[0][n][i];
-          if (p.y_sorted != nullptr) v += routed_sum(p, row, r);
-          const __nv_bfloat16 o = __float2bfloat16_rn(v);
-          p.out_bf16[(size_t)row * p.rows + r] = *reinterpret_cast<const uint16_t*>(&o);
-        }
-      }
-    }
+    epilogue(h);
   }
 }
 
-// Routed-only combine: y[n][r] = sum_j w[n][j] * y_sorted[row_slot[n][j]][r] (einsum "nkd,nk->nd").
+// Weighted sum of the routed slots' outputs (einsum "nkd,nk->nd"), plus an optional f32 addend (the shared
+// expert's output): out[n][r] = sum_j w[n][j] * y_sorted[row_slot[n][j]][r] (+ add[n][r]), written as f32 and/or
+// bf16. Four consecutive r per thread; the slot rows, weights and slot outputs each take one memory round trip.
 __global__ void combine_kernel(const float* __restrict__ y_sorted, const int* __restrict__ row_slot,
-                               const float* __restrict__ wts, int N, int topk, int H, float* __restrict__ y) {
-  const long long total = (long long)N * H;
+                               const float* __restrict__ wts, int N, int topk, int H, const float* __restrict__ add,
+                               float* __restrict__ out_f32, uint16_t* __restrict__ out_bf16) {
+  const int H4 = H / 4;
+  const long long total = (long long)N * H4;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
-    const int n = (int)(i / H), r = (int)(i % H);
-    float v = 0.f;
+    const int n = (int)(i / H4), c4 = (int)(i % H4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int q0 = 0; q0 < topk; q0 += 8) {
       int rs[8];
-      float wt[8], yy[8];
+      float wt[8];
+      float4 yv[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const bool in = q0 + q < topk;
@@ -373,11 +506,32 @@ __global__ void combine_kernel(const float* __restrict__ y_sorted, const int* __
         wt[q] = in ? wts[n * topk + q0 + q] : 0.f;
       }
 #pragma unroll
-      for (int q = 0; q < 8; ++q) yy[q] = rs[q] >= 0 ? y_sorted[(size_t)rs[q] * H + r] : 0.f;
+      for (int q = 0; q < 8; ++q)
+        yv[q] = rs[q] >= 0 ? reinterpret_cast<const float4*>(y_sorted + (size_t)rs[q] * H)[c4]
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) v += wt[q] * yy[q];
+      for (int q = 0; q < 8; ++q) {
+        v.x += wt[q] * yv[q].x;
+        v.y += wt[q] * yv[q].y;
+        v.z += wt[q] * yv[q].z;
+        v.w += wt[q] * yv[q].w;
+      }
     }
-    y[i] = v;
+    if (add != nullptr) {
+      const float4 a = reinterpret_cast<const float4*>(add + (size_t)n * H)[c4];
+      v.x += a.x;
+      v.y += a.y;
+      v.z += a.z;
+      v.w += a.w;
+    }
+    const size_t o = (size_t)n * H4 + c4;
+    if (out_f32 != nullptr) reinterpret_cast<float4*>(out_f32)[o] = v;
+    if (out_bf16 != nullptr) {
+      uint2 pk;
+      pk.x = pack_bf16x2(v.x, v.y);
+      pk.y = pack_bf16x2(v.z, v.w);
+      reinterpret_cast<uint2*>(out_bf16)[o] = pk;
+    }
   }
 }
 
@@ -393,8 +547,9 @@ int launch_decode_t(const DecodeParams& p, int kind, cudaStream_t stream) {
     CBMOE_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecodeThreads, SM::kTotal));
     grid = num_sms() * (per_sm > 0 ? per_sm : 1);
   }
+  const int g = (p.grid_cap > 0 && p.grid_cap < grid) ? p.grid_cap : grid;
   prof_begin(kind, stream);
-  kern<<<grid, kDecodeThreads, SM::kTotal, stream>>>(p);
+  kern<<<g, kDecodeThreads, SM::kTotal, stream>>>(p);
   prof_end(kind, stream);
   CBMOE_CUDA_TRY(cudaGetLastError());
   return CBMOE_OK;
@@ -403,27 +558,30 @@ int launch_decode_t(const DecodeParams& p, int kind, cudaStream_t stream) {
 #ifndef CBMOE_STAGES_CB3
 #define CBMOE_STAGES_CB3 3
 #endif
+#ifndef CBMOE_STAGES_NT1
+#define CBMOE_STAGES_NT1 3
+#endif
 constexpr int kStagesCB3 = CBMOE_STAGES_CB3;
-constexpr int kStagesW8 = 3;
+constexpr int kStagesW8 = 2;   // the W8 kernels run beside the routed ones (side stream): small footprint
 
 template <int FMT, int NMAT, int EPI, int HILO>
 int launch_decode_nt(const DecodeParams& p, int nt, int kind, cudaStream_t stream) {
   constexpr int NS = (FMT == kFmtCB3) ? kStagesCB3 : kStagesW8;
   switch (nt) {
-    case 1: return launch_decode_t<FMT, NMAT, 1, EPI, HILO, NS>(p, kind, stream);
+    case 1: return launch_decode_t<FMT, NMAT, 1, EPI, HILO, CBMOE_STAGES_NT1>(p, kind, stream);
     case 2: return launch_decode_t<FMT, NMAT, 2, EPI, HILO, NS>(p, kind, stream);
     default: return launch_decode_t<FMT, NMAT, 4, EPI, HILO, NS>(p, kind, stream);
   }
 }
 
-int launch_combine(const float* y_sorted, const int* row_slot, const float* wts, int N, int topk, int H, float* y,
-                   cudaStream_t stream) {
-  const long long total = (long long)N * H;
+int launch_combine(const float* y_sorted, const int* row_slot, const float* wts, int N, int topk, int H,
+                   const float* add, float* out_f32, uint16_t* out_bf16, cudaStream_t stream) {
+  const long long total = (long long)N * (H / 4);
   int blocks = (int)((total + 255) / 256);
   if (blocks > num_sms() * 8) blocks = num_sms() * 8;
   if (blocks < 1) blocks = 1;
   prof_begin(kProfCombine, stream);
-  combine_kernel<<<blocks, 256, 0, stream>>>(y_sorted, row_slot, wts, N, topk, H, y);
+  combine_kernel<<<blocks, 256, 0, stream>>>(y_sorted, row_slot, wts, N, topk, H, add, out_f32, out_bf16);
   prof_end(kProfCombine, stream);
   CBMOE_CUDA_TRY(cudaGetLastError());
   return CBMOE_OK;
@@ -442,8 +600,8 @@ int decode_cb3_single(const DecodeParams& p, int nt, cudaStream_t s) {
 int decode_w8_gateup(const DecodeParams& p, int nt, cudaStream_t s) {
   return launch_decode_nt<kFmtW8, 2, kEpiSwiglu, 0>(p, nt, kProfW8GateUp, s);
 }
-int decode_w8_down_combine(const DecodeParams& p, int nt, cudaStream_t s) {
-  return launch_decode_nt<kFmtW8, 1, kEpiCombine, 1>(p, nt, kProfW8DownCombine, s);
+int decode_w8_down_store(const DecodeParams& p, int nt, cudaStream_t s) {
+  return launch_decode_nt<kFmtW8, 1, kEpiStore, 1>(p, nt, kProfW8Down, s);
 }
 int decode_w8_single(const DecodeParams& p, int nt, cudaStream_t s) {
   return launch_decode_nt<kFmtW8, 1, kEpiStore, 0>(p, nt, kProfW8Single, s);

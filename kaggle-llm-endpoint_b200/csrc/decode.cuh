@@ -6,7 +6,6 @@ namespace cbmoe {
 
 constexpr int kEpiSwiglu = 0;
 constexpr int kEpiStore = 1;
-constexpr int kEpiCombine = 2;
 constexpr int kConsumerWarps = kWarpsPerBlock;
 constexpr int kDecodeThreads = (kConsumerWarps + 1) * 32;
 
@@ -29,27 +28,30 @@ struct DecodeParams {
   float limit;
   uint16_t* h_out;          // SWIGLU: [sorted row][2*rows] (per 256 block: hi 256 | lo 256)
   float* y_out;             // STORE: [row][rows]
-  const float* y_sorted;    // COMBINE: routed slot outputs [sorted row][rows] (nullptr: none)
-  const int* row_slot;      //          sorted row of slot (n, j), [N, topk]
-  const float* wts;         //          routing weights [N, topk]
-  int topk;
-  uint16_t* out_bf16;       //          [N][rows]
-  // work distribution
-  int KQ;                   // K splits per (pass, row block): 1, or > 1 with partial sums + last-arriver epilogue
-  int* sched;               // [0] = next-item counter, zero at launch (nullptr: static round-robin over items)
-  int* done;                // KQ > 1: arrival counter per (pass, row block), zero at launch, reset by the last
-  float* part;              // KQ > 1: partial sums [KQ][part_rows][NMAT][rows]
-  int part_rows;
+  // work distribution (decode.cu, Schedule): tickets over whole items, then over pieces of the tail items
+  int grid_cap;             // CTAs to launch at most (0: the resident grid)
+  int* sched;               // [0] = ticket counter, zero at launch (nullptr: static round-robin over tickets)
+  int tail_items;           // tail items the partial-sum space holds
+  int* done;                // arrival counter per item [passes x RB], zero at launch, reset by the last arriver
+  float* part;              // partial sums of the tail items' pieces, [tail_items][Q][8*NT][NMAT][64] f32
+                            // (nullptr: every item whole)
 };
+
+constexpr int kDecodePieces = 4;   // pieces per tail item (at most; KS if smaller)
+
+// Partial-sum space of one decode launch (DecodeParams::part).
+inline size_t decode_part_bytes(int tail_items, int nt, int nmat) {
+  return (size_t)tail_items * kDecodePieces * (8 * nt) * nmat * kRowsPerBlock * sizeof(float);
+}
 
 int decode_cb3_gateup(const DecodeParams& p, int nt, cudaStream_t s);
 int decode_cb3_down(const DecodeParams& p, int nt, cudaStream_t s);
 int decode_cb3_single(const DecodeParams& p, int nt, cudaStream_t s);
 int decode_w8_gateup(const DecodeParams& p, int nt, cudaStream_t s);
-int decode_w8_down_combine(const DecodeParams& p, int nt, cudaStream_t s);
 int decode_w8_single(const DecodeParams& p, int nt, cudaStream_t s);
-int launch_combine(const float* y_sorted, const int* row_slot, const float* wts, int N, int topk, int H, float* y,
-                   cudaStream_t stream);
+int decode_w8_down_store(const DecodeParams& p, int nt, cudaStream_t s);
+int launch_combine(const float* y_sorted, const int* row_slot, const float* wts, int N, int topk, int H,
+                   const float* add, float* out_f32, uint16_t* out_bf16, cudaStream_t stream);
 int launch_route_plan(const int32_t* idx, const float* w, int T, int k, int E, int tm, int pass_tokens,
                       int32_t* plan, cudaStream_t stream, int* zero = nullptr, int n_zero = 0);
 

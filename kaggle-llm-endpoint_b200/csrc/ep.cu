@@ -193,7 +193,8 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
                               size_t workspace_bytes, cudaStream_t stream) {
   if (!ep_args_ok(comm_v, nranks, rank, local, E_total, N_local, k, capacity) || !lyr::shared_ok(sh))
     return CBMOE_ERR_INVALID;
-  if (N_local > 0 && (!x || !idx || !w || !out || !lyr::aligned16(x))) return CBMOE_ERR_INVALID;
+  if (N_local > 0 && (!x || !idx || !w || !out || !lyr::aligned16(x) || !lyr::aligned16(out)))
+    return CBMOE_ERR_INVALID;
   ncclComm_t comm = static_cast<ncclComm_t>(comm_v);
   const int E_loc = local->E, H = local->H, I = local->I;
   const EpWorkspace W = ep_workspace(E_loc, H, I, N_local, k, nranks, capacity);
@@ -212,37 +213,13 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
   const int S = N_local * k;
   int rc = CBMOE_OK;
 
-  // shared expert gate/up of the local tokens on the side stream
+  // shared expert of the local tokens on the side stream (gate/up, down -> ys)
   lyr::SideStream* side = nullptr;
   rc = lyr::side_stream(&side);
   if (rc) return rc;
-  uint16_t* hs = reinterpret_cast<uint16_t*>(wl + W.Wl.hs);
-  int* sched_sh = reinterpret_cast<int*>(wl + W.Wl.sched) + W.Wl.n_zero_routed;
   if (N_local > 0) {
-    CBMOE_CUDA_TRY(cudaEventRecord(side->fork, stream));
-    CBMOE_CUDA_TRY(cudaStreamWaitEvent(side->s, side->fork, 0));
-    CBMOE_CUDA_TRY(cudaMemsetAsync(sched_sh, 0, (size_t)W.Wl.n_zero_shared * 4, side->s));
-    DecodeParams p = lyr::base_params();
-    p.wq = static_cast<const uint8_t*>(sh->gateup_q);
-    p.s0 = sh->gate_s;
-    p.s1 = sh->up_s;
-    p.scale_axis = sh->scale_axis;
-    p.rows = I;
-    p.K = H;
-    p.RB = I / kRowsPerBlock;
-    p.KS = H / kStageK;
-    p.b = x;
-    p.N = N_local;
-    p.limit = limit;
-    p.h_out = hs;
-    p.KQ = W.Wl.kq_sgu;
-    p.sched = sched_sh;
-    p.done = sched_sh + 2;
-    p.part = reinterpret_cast<float*>(wl + W.Wl.part_sgu);
-    p.part_rows = N_local;
-    rc = decode_w8_gateup(p, lyr::decode_nt(N_local), side->s);
+    rc = lyr::shared_side(sh, x, N_local, H, I, limit, wl, W.Wl, side, stream);
     if (rc) return rc;
-    CBMOE_CUDA_TRY(cudaEventRecord(side->join, side->s));
   }
 
   // 1-2. route + pack
@@ -274,8 +251,8 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
     rc = lyr::routed_decode(local, recv_x, W.R, recv_meta, ones, 1, limit, wr, W.Wr, stream);
     if (!rc) {
       const int32_t* plan = reinterpret_cast<const int32_t*>(wr + W.Wr.plan);
-      rc = launch_combine(reinterpret_cast<const float*>(wr + W.Wr.y), plan + W.Wr.L.off[9], ones, W.R, 1, H, y_recv,
-                          stream);
+      rc = launch_combine(reinterpret_cast<const float*>(wr + W.Wr.y), plan + W.Wr.L.off[9], ones, W.R, 1, H,
+                          nullptr, y_recv, nullptr, stream);
     }
   }
   if (rc) goto join;
@@ -284,24 +261,7 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
 join:
   if (N_local > 0) CBMOE_CUDA_TRY(cudaStreamWaitEvent(stream, side->join, 0));
   if (rc || N_local == 0) return rc;
-  // 6. shared down + weighted sum of the returned rows
-  DecodeParams d = lyr::base_params();
-  d.wq = static_cast<const uint8_t*>(sh->down_q);
-  d.s0 = sh->down_s;
-  d.scale_axis = sh->scale_axis;
-  d.rows = H;
-  d.K = I;
-  d.RB = H / kRowsPerBlock;
-  d.KS = I / kStageK;
-  d.b = hs;
-  d.b_hilo = 1;
-  d.N = N_local;
-  d.y_sorted = y_back;
-  d.row_slot = slot_pos;
-  d.wts = w;
-  d.topk = k;
-  d.out_bf16 = out;
-  d.KQ = 1;
-  d.sched = sched_sh + 1;
-  return decode_w8_down_combine(d, lyr::decode_nt(N_local), stream);
+  // 6. weighted sum of the returned rows + the shared expert
+  return launch_combine(y_back, slot_pos, w, N_local, k, H, reinterpret_cast<const float*>(wl + W.Wl.ys), nullptr,
+                        out, stream);
 }

@@ -13,12 +13,15 @@ struct PlanLayoutHost {
 
 // Workspace of the decode path (layout documented at decode_workspace in capi.cu).
 struct DecodeWorkspace {
-  size_t plan, h, y, hs, sched, part_gu, part_sgu, part_sdn, total;
-  int nt, Rp, P, Ps, RB_gu, RB_dn;
-  int kq_gu, kq_sgu, kq_sdn;
-  int n_zero_routed, n_zero_shared;   // words
+  size_t plan, h, y, hs, ys, done, part_gu, part_dn, part_sgu, part_sdn, total;
+  int nt, nt_s, Rp, P, Ps, RB_gu, RB_dn;
+  int tail_gu, tail_dn, tail_sgu, tail_sdn;   // partial-sum space of each launch, in tail items
+  int n_zero_routed, n_zero_shared;           // arrival counters (words)
   PlanLayoutHost L;
 };
+
+// Resident CTAs per SM of the decode kernels are at most this (their shared memory bounds it).
+constexpr int kDecodeMaxCtasPerSm = 4;
 
 struct GroupedWorkspace {
   size_t plan, xs, h, y, hs, sy, total;
@@ -30,6 +33,16 @@ struct SideStream {
   cudaStream_t s = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
 };
+
+// CTAs of the shared-expert kernels, which run on the side stream beside the routed kernels: few enough to leave
+// the routed kernels most of the GPU, enough to finish well within them.
+constexpr int kSideCtas = 24;
+
+// Shared expert of one layer call on the side stream: gate/up (x -> hs, SwiGLU) then down (hs -> ys f32). The
+// counters (n_zero words at `counters`) are zeroed there first. Forks after the caller's prior work on `stream`;
+// the caller joins `side->join` before reading ys.
+int shared_side(const cbmoe_shared* sh, const uint16_t* x, int N, int H, int I, float limit, uint8_t* ws,
+                const DecodeWorkspace& W, SideStream* side, cudaStream_t stream);
 
 size_t align_up(size_t v);
 PlanLayoutHost host_plan_layout(int T, int k, int E, int tm, int pass_tokens);

@@ -12,7 +12,7 @@ enum ProfKind {
   kProfCb3Down = 2,       // decode_kernel_t<CB3, 1 matrix, STORE, hi/lo B>
   kProfCb3Single = 3,     // decode_kernel_t<CB3, 1 matrix, STORE>
   kProfW8GateUp = 4,      // decode_kernel_t<W8, 2 matrices, SWIGLU>
-  kProfW8DownCombine = 5, // decode_kernel_t<W8, 1 matrix, COMBINE>
+  kProfW8Down = 5,        // decode_kernel_t<W8, 1 matrix, STORE, hi/lo B>
   kProfW8Single = 6,      // decode_kernel_t<W8, 1 matrix, STORE>
   kProfCombine = 7,       // combine_kernel
   kProfOther = 8,         // layout repacks, dequant checks, row gathers

@@ -2,7 +2,7 @@
 
 The no-alloc entry point exists for callers that cannot allocate device memory for a workspace (an engine whose
 allocator owns all device memory, a plugin host that forbids allocation during execute, host code that must not
-block on cudaMalloc). It keeps its scratch in a fixed 24 MiB device array inside the library. This file is
+block on cudaMalloc). It keeps its scratch in a fixed 48 MiB device array inside the library. This file is
 collected last on purpose, so a run that stops at the first failure has run every other test before it; it also
 passes when run alone in a fresh process.
 """
@@ -57,7 +57,7 @@ def test_noalloc_rejects_requests_beyond_the_array():
     E, H, I = 160, 5120, 1536
     p = {"E": E, "H": H, "I": I, "gate_up_q": (torch.empty(16, dtype=torch.uint8, device="cuda"),) * 2,
          "down_q": (torch.empty(16, dtype=torch.uint8, device="cuda"),) * 2}
-    N, k = 512, 8                                      # needs ~120 MB of scratch: more than the 24 MiB array
+    N, k = 512, 8                                      # needs ~120 MB of scratch: more than the 48 MiB array
     x = torch.zeros((N, H), dtype=torch.bfloat16, device="cuda")
     idx = torch.zeros((N, k), dtype=torch.int32, device="cuda")
     w = torch.zeros((N, k), dtype=torch.float32, device="cuda")
