@@ -74,10 +74,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait_sleepy(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
-  uint32_t ns = 64;
+  uint32_t ns = 32;
   while (!mbar_try_wait(bar, parity)) {
     __nanosleep(ns);
-    if (ns < 1024) ns <<= 1;
+    if (ns < 256) ns <<= 1;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       atomicOr(&g_device_errors, CBMOE_DEVERR_TIMEOUT);
       return false;
