@@ -57,8 +57,11 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="resident layers cycled by the steps (profiling "
                     "captures use 1 to keep device memory small)")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
-                    help="decode = config 1 (the default bench line); prefill = config 3 (4096 tokens, tcgen05 path)")
+    ap.add_argument("--workload", choices=["decode", "prefill", "ep"], default="decode",
+                    help="decode = config 1 (the default bench line); prefill = config 3 (4096 tokens, tcgen05 path); "
+                         "ep = config 4 (4 layers, 256 tokens, experts sharded over the GPUs, strong scaling)")
+    ap.add_argument("--ep-path", choices=["auto", "decode", "grouped"], default="auto",
+                    help="expert kernels of --workload ep at N = 1 (N > 1 picks by received rows)")
     return ap.parse_args()
 
 
@@ -174,6 +177,17 @@ def make_batches(torch, dev, seed, n_batches):
         w = torch.softmax(top, dim=-1)
         out.append((x, idx.to(torch.int32).contiguous(), w.contiguous()))
     return out
+
+
+def ep_capacity(slots, world):
+    """Rows per peer in each direction of the expert-parallel exchange: with uniform routing a peer's share of a
+    rank's slots is Binomial(slots, 1/world); mean + 4 sigma + 16 rows (slots beyond it would be dropped and
+    flagged in cbmoe_device_errors)."""
+    import math
+    if world <= 1:
+        return slots
+    p = 1.0 / world
+    return min(slots, int(math.ceil(slots * p + 4.0 * math.sqrt(slots * p * (1 - p)))) + 16)
 
 
 # ------------------------------------------------------------------------------------------------ CPU legs
@@ -339,8 +353,7 @@ def run_ours(args):
     batches = make_batches(torch, dev, 7 + rank, N_BATCHES)
     fetch = cbmoe.ResidentFetch(path="decode")
     out = torch.empty((N_TOK, H), dtype=torch.bfloat16, device=dev)
-    # rows per peer in each direction: 4x the mean share of a rank's slots (uniform routing), at least 16
-    cap = min(N_TOK * TOPK, max(16, 4 * N_TOK * TOPK // max(world, 1)))
+    cap = ep_capacity(N_TOK * TOPK, world)
     torch.cuda.synchronize()
 
     def step(s):
@@ -588,10 +601,164 @@ def run_prefill(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------ config 4
+T_EP, L_EP = 256, 4
+
+
+def run_ep_stack(args):
+    """Config 4: 4 MoE layers of the config-1 shape on 256 tokens (uniform top-8), the 160 experts sharded over the
+    N GPUs (expert parallelism, NCCL dispatch and return); every rank holds 256/N of the tokens. Strong scaling: the
+    global batch is the same at every N. N = 1 runs the same 4 layers through the single-GPU layer call."""
+    import torch
+    import torch.distributed as dist
+    import cbmoe
+    from cbmoe._lib import launch_count
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    assert T_EP % world == 0 and E % world == 0, (T_EP, E, world)
+    t_loc = T_EP // world
+    group = None
+    layers = []
+    if world > 1:
+        from cbmoe.ep import ExpertParallel
+        group = ExpertParallel()
+        for li in range(L_EP):
+            full, _ = make_layer_tables(torch, 3000 + li, dev)
+            layers.append(group.pack_local(*full))
+            del full
+    else:
+        layers = [make_layer(torch, cbmoe, 3000 + li, dev)[0] for li in range(L_EP)]
+    # the same global batches at every N: generated from one seed, each rank keeps its token rows
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    n_batches = 8
+    batches = []
+    for _ in range(n_batches):
+        x = torch.randn((T_EP, H), device=dev, generator=g).to(torch.bfloat16)
+        routes = []
+        for _ in range(L_EP):
+            logits = torch.randn((T_EP, E), device=dev, generator=g)
+            top, idx = torch.topk(logits, TOPK, dim=-1)
+            w = torch.softmax(top, dim=-1)
+            sl = slice(rank * t_loc, (rank + 1) * t_loc)
+            routes.append((idx[sl].to(torch.int32).contiguous(), w[sl].contiguous()))
+        batches.append((x[rank * t_loc:(rank + 1) * t_loc].contiguous(), routes))
+    path = args.ep_path
+    fetch = cbmoe.ResidentFetch(path=path)
+    cap = ep_capacity(t_loc * TOPK, world)
+    bufs = [torch.empty((t_loc, H), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+
+    def stack(x, routes):
+        for li in range(L_EP):
+            idx, w = routes[li]
+            out = bufs[li % 2]
+            if group is not None:
+                group.layer(layers[li], x, idx, w, LIMIT, capacity=cap, out=out)
+            else:
+                fetch.layer(layers[li], x, idx, w, LIMIT, out=out)
+            x = out
+        return x
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_ms(ms):
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    for s in range(args.warmup):
+        stack(*batches[s % n_batches])
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = launch_count()
+    with ClockSampler(local) as clocks:
+        ev0.record()
+        for s in range(args.steps):
+            stack(*batches[(args.warmup + s) % n_batches])
+        ev1.record()
+        torch.cuda.synchronize()
+    launches = launch_count() - l0
+    ms = max_ms(ev0.elapsed_time(ev1))
+    barrier()
+    value = T_EP * args.steps / (ms / 1000.0)
+
+    # e2e: this rank's token rows and its 4 layers' routing from pinned host memory, the output back, every step
+    host = [(x.cpu().pin_memory(), [(i.cpu().pin_memory(), w.cpu().pin_memory()) for i, w in r]) for x, r in batches]
+    xd = torch.empty((t_loc, H), dtype=torch.bfloat16, device=dev)
+    rd = [(torch.empty((t_loc, TOPK), dtype=torch.int32, device=dev),
+           torch.empty((t_loc, TOPK), dtype=torch.float32, device=dev)) for _ in range(L_EP)]
+    out_h = torch.empty((t_loc, H), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step(s):
+        xh, rh = host[s % n_batches]
+        xd.copy_(xh, non_blocking=True)
+        for (i_d, w_d), (i_h, w_h) in zip(rd, rh):
+            i_d.copy_(i_h, non_blocking=True)
+            w_d.copy_(w_h, non_blocking=True)
+        out_h.copy_(stack(xd, rd), non_blocking=True)
+
+    for s in range(args.warmup):
+        e2e_step(s)
+    barrier()
+    ev0.record()
+    for s in range(args.steps):
+        e2e_step(args.warmup + s)
+    ev1.record()
+    torch.cuda.synchronize()
+    ms_e2e = max_ms(ev0.elapsed_time(ev1))
+    e2e = T_EP * args.steps / (ms_e2e / 1000.0)
+    # per-kernel event times (a separate pass: events between kernels), rank 0's view
+    from cbmoe._lib import profile_enable, profile_read
+    profile_read(reset=True)
+    profile_enable(True)
+    for s in range(args.steps):
+        stack(*batches[(args.warmup + s) % n_batches])
+    torch.cuda.synchronize()
+    profile_enable(False)
+    prof = profile_read(reset=True)
+    kern = {k: {"launches": n, "avg_us": 1000 * t / n, "ms_per_step": t / args.steps} for k, (n, t) in prof.items()}
+    h2d = t_loc * H * 2 + L_EP * t_loc * TOPK * 8
+    d2h = t_loc * H * 2
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "config4: 4 MoE layers of the config-1 shape, 256 tokens, uniform top-8, "
+                                       "160 CB3 experts sharded over the GPUs + replicated int8 shared expert",
+                           "global_batch": T_EP, "tokens_per_gpu": t_loc, "layers": L_EP,
+                           "experts_per_gpu": E // world, "capacity_rows_per_peer": cap if world > 1 else None,
+                           "path": path, "parallelism": f"expert parallel x{world}" if world > 1 else "single GPU",
+                           "l2": "4 resident layers (1.47 GB each) per step: inputs larger than L2"},
+                "clocks": clocks.summary(), "gpu_launches": launches,
+                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d * world,
+                        "d2h_bytes_per_step": d2h * world, "ms_per_step": ms_e2e / args.steps},
+                "kernels": kern, "cpu_baseline": None, "device_errors": cbmoe.device_errors(clear=True)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        group.close()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.workload == "prefill" and args.impl == "ours":
         run_prefill(args)
+        return
+    if args.workload == "ep" and args.impl == "ours":
+        run_ep_stack(args)
         return
     if args.impl == "reference":
         run_reference(args)

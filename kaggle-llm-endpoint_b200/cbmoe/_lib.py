@@ -119,7 +119,7 @@ def device_errors(clear=True):
 
 
 PROFILE_KINDS = ("plan", "cb3_gateup", "cb3_down", "cb3_single", "w8_gateup", "w8_down", "w8_single",
-                 "combine", "other", "grp_cb3_gateup", "grp_cb3_down", "grp_w8_gateup", "grp_w8_store")
+                 "combine", "other", "grp_cb3_gateup", "grp_cb3_down", "grp_w8_gateup", "grp_w8_store", "exchange")
 
 
 def profile_enable(on=True):

@@ -31,7 +31,10 @@ int decode_nt(int N) { return N <= 8 ? 1 : (N <= 16 ? 2 : 4); }
 // larger passes cost shared memory and occupancy on every item).
 int decode_nt_routed(int N, int k, int E) {
   const long long S = (long long)N * k;
-  return S <= 2LL * E ? 1 : (S <= 6LL * E ? 2 : 4);
+#ifndef CBMOE_NT2_SLOTS_PER_EXPERT
+#define CBMOE_NT2_SLOTS_PER_EXPERT 6
+#endif
+  return S <= 2LL * E ? 1 : (S <= (long long)CBMOE_NT2_SLOTS_PER_EXPERT * E ? 2 : 4);
 }
 
 // Workspace of the decode path:
@@ -46,9 +49,9 @@ int decode_tail_items(long long items) {
   return (int)(items < half ? items : half);
 }
 
-DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k) {
+DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k, long long slots_hint) {
   DecodeWorkspace w;
-  w.nt = decode_nt_routed(N, k, E);
+  w.nt = slots_hint >= 0 ? decode_nt_routed((int)(slots_hint < N ? slots_hint : N), 1, E) : decode_nt_routed(N, k, E);
   w.nt_s = decode_nt(N);
   const int pt = 8 * w.nt;
   w.L = host_plan_layout(N, k, E, 1, pt);
@@ -179,6 +182,35 @@ int shared_side(const cbmoe_shared* sh, const uint16_t* x, int N, int H, int I, 
   int* done_sh = reinterpret_cast<int*>(ws + W.done) + W.n_zero_routed;
   CBMOE_CUDA_TRY(cudaMemsetAsync(done_sh, 0, (size_t)W.n_zero_shared * 4, side->s));
   uint16_t* hs = reinterpret_cast<uint16_t*>(ws + W.hs);
+  if (N > kW8DecodeMaxTokens && H % kGrpTileM == 0 && I % kGrpTileM == 0) {
+    // enough tokens for the tensor-core kernels (h as plain bf16 [N][I] in the same region)
+    GroupedParams g{};
+    g.wq = static_cast<const uint8_t*>(sh->gateup_q);
+    g.s0 = sh->gate_s;
+    g.s1 = sh->up_s;
+    g.scale_axis = sh->scale_axis;
+    g.rows = I;
+    g.K = H;
+    g.N = N;
+    g.E = 1;
+    g.limit = limit;
+    g.out = hs;
+    int rc = grouped_w8_gateup(g, x, N, side->s);
+    if (rc) return rc;
+    GroupedParams gd{};
+    gd.wq = static_cast<const uint8_t*>(sh->down_q);
+    gd.s0 = sh->down_s;
+    gd.scale_axis = sh->scale_axis;
+    gd.rows = H;
+    gd.K = I;
+    gd.N = N;
+    gd.E = 1;
+    gd.out_f32 = reinterpret_cast<float*>(ws + W.ys);
+    rc = grouped_w8_store_f32(gd, hs, N, side->s);
+    if (rc) return rc;
+    CBMOE_CUDA_TRY(cudaEventRecord(side->join, side->s));
+    return CBMOE_OK;
+  }
 
   DecodeParams p = base_params();
   p.wq = static_cast<const uint8_t*>(sh->gateup_q);
@@ -225,9 +257,10 @@ int shared_side(const cbmoe_shared* sh, const uint16_t* x, int N, int H, int I, 
 }
 
 // Slots (N*k) above which CBMOE_PATH_AUTO takes the grouped tensor-core path.
-constexpr int kGroupedMinSlots = 1024;
-// Token rows above which cbmoe_w8_linear runs the tcgen05 GEMM instead of the decode kernel.
-constexpr int kW8DecodeMaxTokens = 64;
+#ifndef CBMOE_GROUPED_MIN_SLOTS
+#define CBMOE_GROUPED_MIN_SLOTS 1024
+#endif
+constexpr int kGroupedMinSlots = CBMOE_GROUPED_MIN_SLOTS;
 
 int pick_path(int N, int k, int path) {
   if (path != CBMOE_PATH_AUTO) return path;

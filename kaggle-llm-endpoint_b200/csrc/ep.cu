@@ -111,13 +111,17 @@ EpWorkspace ep_workspace(int E_loc, int H, int I, int N_local, int k, int nranks
   w.sub_local = w.y_back + align_up((size_t)w.R * H * 4);
   w.Wl = lyr::decode_workspace(E_loc, H, I, N_local, k);
   w.sub_recv = w.sub_local + align_up(w.Wl.total);
-  w.recv_path = lyr::pick_path(w.R, 1, CBMOE_PATH_AUTO);
+  // The receive buffer holds up to R rows, but a rank expects about its own slot count (N_local * k) of real
+  // ones: the kernels are chosen by that, tensor-core GEMMs from 8 rows per local expert on.
+  const long long expect = (long long)N_local * k;
+  w.recv_path = (expect >= 8LL * E_loc && H % kGrpTileM == 0 && I % kGrpTileM == 0) ? CBMOE_PATH_GROUPED
+                                                                                   : CBMOE_PATH_DECODE;
   size_t rb = 0;
   if (w.recv_path == CBMOE_PATH_GROUPED) {
     w.Gr = lyr::grouped_workspace(E_loc, H, I, w.R, 1);
     rb = w.Gr.total;
   } else {
-    w.Wr = lyr::decode_workspace(E_loc, H, I, w.R, 1);
+    w.Wr = lyr::decode_workspace(E_loc, H, I, w.R, 1, expect);
     rb = w.Wr.total;
   }
   w.total = w.sub_recv + align_up(rb);
@@ -226,18 +230,23 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
   prof_begin(kProfOther, stream);
   ep_route_kernel<<<1, kEpThreads, 0, stream>>>(idx, S, E_total, E_loc, nranks, capacity, send_meta, slot_pos, ones,
                                                 W.R);
+  prof_end(kProfOther, stream);
+  CBMOE_CUDA_TRY(cudaGetLastError());
   if (S > 0) {
+    prof_begin(kProfOther, stream);
     const long long total = (long long)S * (H / 8);
     int blocks = (int)((total + 255) / 256);
     if (blocks > num_sms() * 8) blocks = num_sms() * 8;
     ep_pack_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const uint4*>(x), H / 8, slot_pos, S, k,
                                                reinterpret_cast<uint4*>(send_x));
+    prof_end(kProfOther, stream);
+    CBMOE_CUDA_TRY(cudaGetLastError());
   }
-  prof_end(kProfOther, stream);
-  CBMOE_CUDA_TRY(cudaGetLastError());
   // 3. dispatch
+  prof_begin(kProfExchange, stream);
   rc = exchange(comm, nranks, rank, send_x, recv_x, (size_t)capacity * H, ncclBfloat16, 2, stream);
   if (!rc) rc = exchange(comm, nranks, rank, send_meta, recv_meta, (size_t)capacity, ncclInt32, 4, stream);
+  prof_end(kProfExchange, stream);
   if (rc) goto join;
   // 4. local experts on the received rows (one slot per row, weight 1)
   if (W.recv_path == CBMOE_PATH_GROUPED) {
@@ -257,7 +266,9 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
   }
   if (rc) goto join;
   // 5. return the expert outputs
+  prof_begin(kProfExchange, stream);
   rc = exchange(comm, nranks, rank, y_recv, y_back, (size_t)capacity * H, ncclFloat32, 4, stream);
+  prof_end(kProfExchange, stream);
 join:
   if (N_local > 0) CBMOE_CUDA_TRY(cudaStreamWaitEvent(stream, side->join, 0));
   if (rc || N_local == 0) return rc;

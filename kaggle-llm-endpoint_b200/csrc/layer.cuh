@@ -36,7 +36,13 @@ struct SideStream {
 
 // CTAs of the shared-expert kernels, which run on the side stream beside the routed kernels: few enough to leave
 // the routed kernels most of the GPU, enough to finish well within them.
-constexpr int kSideCtas = 24;
+#ifndef CBMOE_SIDE_CTAS
+#define CBMOE_SIDE_CTAS 48
+#endif
+constexpr int kSideCtas = CBMOE_SIDE_CTAS;
+// Token rows above which the int8 kernels (cbmoe_w8_linear, the shared expert) run the tcgen05 GEMM instead of
+// the decode kernel.
+constexpr int kW8DecodeMaxTokens = 64;
 
 // Shared expert of one layer call on the side stream: gate/up (x -> hs, SwiGLU) then down (hs -> ys f32). The
 // counters (n_zero words at `counters`) are zeroed there first. Forks after the caller's prior work on `stream`;
@@ -48,7 +54,8 @@ size_t align_up(size_t v);
 PlanLayoutHost host_plan_layout(int T, int k, int E, int tm, int pass_tokens);
 int decode_nt(int N);
 int decode_nt_routed(int N, int k, int E);
-DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k);
+// slots_hint: the slots expected to be real when N*k counts empty ones too (< 0: N*k); picks the token tile.
+DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k, long long slots_hint = -1);
 GroupedWorkspace grouped_workspace(int E, int H, int I, int N, int k);
 int pick_path(int N, int k, int path);
 bool aligned16(const void* p);

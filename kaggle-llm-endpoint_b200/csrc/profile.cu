@@ -39,7 +39,7 @@ cudaEvent_t take_event() {
 
 void prof_begin(int kind, cudaStream_t s) {
   std::lock_guard<std::mutex> lk(g_mu);
-  ++g_launches;
+  if (kind != kProfExchange) ++g_launches;   // an exchange is NCCL's work, not a launch of this library
   if (!g_enabled) return;
   t_open = {kind, take_event(), take_event()};
   cudaEventRecord(t_open.a, s);

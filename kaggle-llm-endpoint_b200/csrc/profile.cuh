@@ -20,6 +20,7 @@ enum ProfKind {
   kProfGrpCb3Down = 10,   // grouped_kernel<CB3, down, STORE>
   kProfGrpW8GateUp = 11,  // grouped_kernel<W8, gate+up, SWIGLU>
   kProfGrpW8Store = 12,   // grouped_kernel<W8, one matrix, STORE>
+  kProfExchange = 13,     // expert-parallel NCCL dispatch or return (one send/recv group)
   kProfKinds = 16
 };
 
