@@ -528,14 +528,23 @@ def run_prefill(args):
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     n_layers = max(1, min(args.layers, 2))
-    layers = [make_layer(torch, cbmoe, 2000 + i, dev)[0] for i in range(n_layers)]
+    made = [make_layer(torch, cbmoe, 2000 + i, dev, keep_std=(i == 0 and not args.no_cpu_baseline))
+            for i in range(n_layers)]
+    layers = [m[0] for m in made]
+    std0 = made[0][1]
+    del made
     g = torch.Generator(device=dev)
     g.manual_seed(5)
+
+    raw_proj = []   # layer 0's QKV and O leaves, for the CPU baseline
 
     def q8(n_in, n_out):
         w = torch.randn((n_in, n_out), device=dev, generator=g) * 0.02
         sc = torch.clamp(w.abs().amax(dim=0, keepdim=True), min=1e-12) / 127.0
-        return cbmoe.ops.pack_w8(torch.clamp(torch.round(w / sc), -127, 127).to(torch.int8)), sc.reshape(-1).contiguous()
+        q = torch.clamp(torch.round(w / sc), -127, 127).to(torch.int8)
+        if len(raw_proj) < 2 and not args.no_cpu_baseline:
+            raw_proj.append((q.cpu().numpy(), sc.cpu().numpy()))
+        return cbmoe.ops.pack_w8(q), sc.reshape(-1).contiguous()
     projs = [(q8(H, QKV_OUT), q8(QKV_OUT, H)) for _ in range(n_layers)]
     x = torch.randn((T_PREFILL, H), device=dev, generator=g).to(torch.bfloat16)
     logits = torch.randn((T_PREFILL, E), device=dev, generator=g)
@@ -586,6 +595,55 @@ def run_prefill(args):
             kern[name] = {"launches": n, "avg_us": 1000 * tms / n, "tflops": per / (tms / n / 1000) / 1e12}
     step_flops = sum(flops.values())
     dom = "grp_cb3_gateup"
+
+    # e2e: the batch's activations and routing from pinned host memory, the layer output back, every step
+    xh, ih, wh = x.cpu().pin_memory(), idx.cpu().pin_memory(), w.cpu().pin_memory()
+    out_h = torch.empty((T_PREFILL, H), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step(s):
+        x.copy_(xh, non_blocking=True)
+        idx.copy_(ih, non_blocking=True)
+        w.copy_(wh, non_blocking=True)
+        step(s)
+        out_h.copy_(out, non_blocking=True)
+
+    for s in range(args.warmup):
+        e2e_step(s)
+    torch.cuda.synchronize()
+    ev0.record()
+    for s in range(args.steps):
+        e2e_step(args.warmup + s)
+    ev1.record()
+    torch.cuda.synchronize()
+    ms_e2e = ev0.elapsed_time(ev1) / args.steps
+    h2d = T_PREFILL * H * 2 + T_PREFILL * TOPK * 8
+    d2h = T_PREFILL * H * 2
+
+    # CPU baseline: QKV + O (int8 dequant + fp32 dot, NumPy) and the layer (C oracle) on a bounded token sample
+    cpu_baseline = None
+    if not args.no_cpu_baseline:
+        import numpy as np
+        from oracle import cpu, q8 as oq8
+        cpu.build()
+        std_np = std_to_numpy(std0)
+        threads = cpu_threads()
+        xs = x.float().cpu().numpy()
+        ids, wts = idx.cpu().numpy(), w.cpu().numpy()
+        (qq, qs), (oq, osc) = raw_proj[0], raw_proj[1]
+        w_qkv = oq8.dequant(qq, qs).astype(np.float32)   # the bf16 weights dequant_tree yields, once (load time)
+        w_o = oq8.dequant(oq, osc).astype(np.float32)
+        n, t_total = 0, 0.0
+        while t_total < args.cpu_seconds and n < 256:
+            t0 = time.perf_counter()
+            qkv_c = xs[n:n + 1] @ w_qkv
+            att_c = qkv_c @ w_o
+            cpu.moe_layer(att_c, ids[n:n + 1], wts[n:n + 1], std_np["gate"], std_np["up"], std_np["down"],
+                          std_np["shared"], LIMIT, threads=threads)
+            t_total += time.perf_counter() - t0
+            n += 1
+        cpu_baseline = {"value": n / t_total, "unit": "tok/s", "cores": threads, "kind": "port",
+                        "sample": f"{n} token(s) of the batch, one at a time: QKV + O on the dequantized int8 leaves (NumPy "
+                                  f"fp32) and the MoE layer (C oracle, OpenMP)"}
     line = {"metric": METRIC, "value": T_PREFILL / (ms / 1000), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -597,7 +655,10 @@ def run_prefill(args):
             "roofline": {"bound": "tensor", "kernel": dom, "achieved": kern[dom]["tflops"], "peak": sustained,
                          "unit": "TFLOP/s", "frac": kern[dom]["tflops"] / sustained,
                          "peak_source": f"{kind} bf16_tflops_sustained (burst {burst})", "traffic": None},
-            "kernels": kern, "profile": {k: (v[0], round(v[1], 3)) for k, v in prof.items()}}
+            "e2e": {"value": T_PREFILL / (ms_e2e / 1000), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
+            "kernels": kern, "profile": {k: (v[0], round(v[1], 3)) for k, v in prof.items()},
+            "cpu_baseline": cpu_baseline}
     print(json.dumps(line), flush=True)
 
 

@@ -49,10 +49,15 @@ int cbmoe_device_errors(int clear, int* out_host);
 int cbmoe_num_sms(void);
 /* Kernels this library has launched in this process (host-side counter). */
 long long cbmoe_launch_count(void);
+/* No counterpart in the reference. Self-test of the kernels' bounded waits: one CTA waits on a barrier phase that
+ * nothing completes, gives up after limit_ns (0 < limit_ns <= 10 s), records CBMOE_DEVERR_TIMEOUT in
+ * cbmoe_device_errors and writes 1 to *gave_up_device (device int). The context stays usable afterwards. */
+int cbmoe_selftest_wait_timeout(long long limit_ns, int* gave_up_device, cudaStream_t stream);
 /* Per-kernel CUDA-event timing: when enabled, every launch is bracketed by two events on its stream.
  * cbmoe_profile_read synchronizes on the recorded events and writes, per kernel kind (n_kinds >= 16 slots:
- * 0 plan, 1 CB3 gate/up, 2 CB3 down, 3 CB3 single, 4 int8 gate/up, 5 int8 down+combine, 6 int8 single,
- * 7 combine, 8 other), the summed milliseconds and launch counts; reset != 0 clears them. */
+ * 0 plan, 1 CB3 gate/up, 2 CB3 down, 3 CB3 single, 4 int8 gate/up, 5 int8 down, 6 int8 single, 7 combine,
+ * 8 other, 9-12 grouped CB3 gate/up, CB3 down, int8 gate/up, int8 store, 13 expert-parallel exchange), the
+ * summed milliseconds and launch counts; reset != 0 clears them. */
 int cbmoe_profile_enable(int enable);
 int cbmoe_profile_read(int reset, double* ms_host, long long* count_host, int n_kinds);
 

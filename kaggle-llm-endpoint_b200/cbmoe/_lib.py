@@ -37,6 +37,7 @@ SIGNATURES = {
     "cbmoe_launch_count": (ctypes.c_longlong, []),
     "cbmoe_profile_enable": (c_int, [c_int]),
     "cbmoe_profile_read": (c_int, [c_int, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong), c_int]),
+    "cbmoe_selftest_wait_timeout": (c_int, [ctypes.c_longlong, c_void_p, c_void_p]),
     "cbmoe_cb3k_idx_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "cbmoe_cb3k_cb_bytes": (c_size_t, [c_int, c_int, c_int]),
     "cbmoe_cb3k_repack": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,

@@ -183,7 +183,8 @@ int shared_side(const cbmoe_shared* sh, const uint16_t* x, int N, int H, int I, 
   CBMOE_CUDA_TRY(cudaMemsetAsync(done_sh, 0, (size_t)W.n_zero_shared * 4, side->s));
   uint16_t* hs = reinterpret_cast<uint16_t*>(ws + W.hs);
   if (N > kW8DecodeMaxTokens && H % kGrpTileM == 0 && I % kGrpTileM == 0) {
-    // enough tokens for the tensor-core kernels (h as plain bf16 [N][I] in the same region)
+    // Enough tokens for the tensor-core kernels (h as plain bf16 [N][I] in the same region).
+    cudaStream_t ss = side->s;
     GroupedParams g{};
     g.wq = static_cast<const uint8_t*>(sh->gateup_q);
     g.s0 = sh->gate_s;
@@ -195,7 +196,7 @@ int shared_side(const cbmoe_shared* sh, const uint16_t* x, int N, int H, int I, 
     g.E = 1;
     g.limit = limit;
     g.out = hs;
-    int rc = grouped_w8_gateup(g, x, N, side->s);
+    int rc = grouped_w8_gateup(g, x, N, ss);
     if (rc) return rc;
     GroupedParams gd{};
     gd.wq = static_cast<const uint8_t*>(sh->down_q);
@@ -206,7 +207,7 @@ int shared_side(const cbmoe_shared* sh, const uint16_t* x, int N, int H, int I, 
     gd.N = N;
     gd.E = 1;
     gd.out_f32 = reinterpret_cast<float*>(ws + W.ys);
-    rc = grouped_w8_store_f32(gd, hs, N, side->s);
+    rc = grouped_w8_store_f32(gd, hs, N, ss);
     if (rc) return rc;
     CBMOE_CUDA_TRY(cudaEventRecord(side->join, side->s));
     return CBMOE_OK;

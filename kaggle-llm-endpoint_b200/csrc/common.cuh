@@ -56,12 +56,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Wait until the phase with the given parity has completed. Returns false (and records CBMOE_DEVERR_TIMEOUT) if
 // that takes longer than kWaitLimitNs; callers then stop issuing work and return.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
-    if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) {
       atomicOr(&g_device_errors, CBMOE_DEVERR_TIMEOUT);
       return false;
     }

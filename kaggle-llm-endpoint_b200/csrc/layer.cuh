@@ -44,9 +44,9 @@ constexpr int kSideCtas = CBMOE_SIDE_CTAS;
 // the decode kernel.
 constexpr int kW8DecodeMaxTokens = 64;
 
-// Shared expert of one layer call on the side stream: gate/up (x -> hs, SwiGLU) then down (hs -> ys f32). The
-// counters (n_zero words at `counters`) are zeroed there first. Forks after the caller's prior work on `stream`;
-// the caller joins `side->join` before reading ys.
+// Shared expert of one layer call on the side stream (forked after the caller's prior work on `stream`, its
+// counters zeroed there first): gate/up (x -> hs, SwiGLU) then down (hs -> ys f32), by the decode kernels up to
+// kW8DecodeMaxTokens tokens and the tensor-core kernels above. The caller joins `side->join` before reading ys.
 int shared_side(const cbmoe_shared* sh, const uint16_t* x, int N, int H, int I, float limit, uint8_t* ws,
                 const DecodeWorkspace& W, SideStream* side, cudaStream_t stream);
 

@@ -455,6 +455,7 @@ int launch_route_plan(const int32_t* idx, const float* w, int T, int k, int E, i
                                                              n_zero);
     plan_place_kernel<<<n_chunks, kPlanCtaWarps * 32, csmem, stream>>>(idx, w, (int)S, k, E, plan, L, chunk);
     prof_end(kProfPlan, stream);
+    prof_add_launches(2);
     CBMOE_CUDA_TRY(cudaGetLastError());
     return CBMOE_OK;
   }

@@ -6,6 +6,7 @@
 #include <vector>
 
 #include "profile.cuh"
+#include "common.cuh"
 
 namespace cbmoe {
 namespace {
@@ -43,6 +44,11 @@ void prof_begin(int kind, cudaStream_t s) {
   if (!g_enabled) return;
   t_open = {kind, take_event(), take_event()};
   cudaEventRecord(t_open.a, s);
+}
+
+void prof_add_launches(int n) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_launches += n;
 }
 
 void prof_end(int kind, cudaStream_t s) {
@@ -90,4 +96,30 @@ extern "C" int cbmoe_profile_read(int reset, double* ms_host, long long* count_h
     }
   }
   return CBMOE_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ self-test
+namespace cbmoe {
+namespace {
+// One CTA waits, through the kernels' own bounded wait, on an mbarrier phase that nothing completes. The wait
+// gives up after limit_ns, records CBMOE_DEVERR_TIMEOUT and the kernel returns: the path every ring wait takes
+// when a producer or a peer never delivers.
+__global__ void wait_selftest_kernel(unsigned long long limit_ns, int* gave_up) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *gave_up = mbar_wait(&bar, 0, limit_ns) ? 0 : 1;
+}
+}  // namespace
+}  // namespace cbmoe
+
+extern "C" int cbmoe_selftest_wait_timeout(long long limit_ns, int* gave_up_device, cudaStream_t stream) {
+  if (limit_ns <= 0 || limit_ns > 10000000000LL || !gave_up_device) return CBMOE_ERR_INVALID;
+  cbmoe::prof_begin(cbmoe::kProfOther, stream);
+  cbmoe::wait_selftest_kernel<<<1, 32, 0, stream>>>((unsigned long long)limit_ns, gave_up_device);
+  cbmoe::prof_end(cbmoe::kProfOther, stream);
+  return cudaGetLastError() == cudaSuccess ? CBMOE_OK : CBMOE_ERR_CUDA;
 }

@@ -26,5 +26,7 @@ enum ProfKind {
 
 void prof_begin(int kind, cudaStream_t s);
 void prof_end(int kind, cudaStream_t s);
+// Launches counted besides the one prof_begin counts (a kind timed as one span over several kernels).
+void prof_add_launches(int n);
 
 }  // namespace cbmoe
