@@ -61,7 +61,7 @@ def parse():
                     help="decode = config 1 (the default bench line); prefill = config 3 (4096 tokens, tcgen05 path); "
                          "ep = config 4 (4 layers, 256 tokens, experts sharded over the GPUs, strong scaling)")
     ap.add_argument("--ep-path", choices=["auto", "decode", "grouped"], default="auto",
-                    help="expert kernels of --workload ep at N = 1 (N > 1 picks by received rows)")
+                    help="expert kernels of --workload ep (N > 1: for the rows each rank receives)")
     return ap.parse_args()
 
 
@@ -654,7 +654,8 @@ def run_prefill(args):
             "step_tflops": step_flops / (ms / 1000) / 1e12,
             "roofline": {"bound": "tensor", "kernel": dom, "achieved": kern[dom]["tflops"], "peak": sustained,
                          "unit": "TFLOP/s", "frac": kern[dom]["tflops"] / sustained,
-                         "peak_source": f"{kind} bf16_tflops_sustained (burst {burst})", "traffic": None},
+                         "peak_source": f"{kind} bf16_tflops_sustained (burst {burst})",
+                         "traffic": load_traffic().get(dom)},
             "e2e": {"value": T_PREFILL / (ms_e2e / 1000), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
             "kernels": kern, "profile": {k: (v[0], round(v[1], 3)) for k, v in prof.items()},
@@ -721,7 +722,7 @@ def run_ep_stack(args):
             idx, w = routes[li]
             out = bufs[li % 2]
             if group is not None:
-                group.layer(layers[li], x, idx, w, LIMIT, capacity=cap, out=out)
+                group.layer(layers[li], x, idx, w, LIMIT, capacity=cap, out=out, path=path)
             else:
                 fetch.layer(layers[li], x, idx, w, LIMIT, out=out)
             x = out

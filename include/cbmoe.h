@@ -174,10 +174,13 @@ int cbmoe_w8_linear(const void* qk, const float* s, int scale_axis, int rows, in
 int cbmoe_ep_unique_id(uint8_t* id128_host);
 int cbmoe_ep_comm_init(const uint8_t* id128_host, int nranks, int rank, void** comm_out);
 int cbmoe_ep_comm_destroy(void* comm);
-size_t cbmoe_ep_workspace_bytes(const cbmoe_experts* local, int N_local, int k, int nranks, int capacity);
+size_t cbmoe_ep_workspace_bytes(const cbmoe_experts* local, int N_local, int k, int nranks, int capacity, int path);
+/* path: kernels for the received rows (CBMOE_PATH_DECODE, CBMOE_PATH_GROUPED, or CBMOE_PATH_AUTO: grouped from 8
+ * expected rows per local expert, N_local * k >= 8 * local->E). */
 int cbmoe_ep_layer(void* comm, int nranks, int rank, const cbmoe_experts* local, int E_total, const cbmoe_shared* sh,
                    const uint16_t* x, int N_local, const int32_t* idx, const float* w, int k, float limit,
-                   int capacity, uint16_t* out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+                   int capacity, int path, uint16_t* out, void* workspace, size_t workspace_bytes,
+                   cudaStream_t stream);
 
 #ifdef __cplusplus
 }

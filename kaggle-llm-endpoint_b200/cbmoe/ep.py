@@ -15,7 +15,7 @@ import ctypes
 import torch
 import torch.distributed as dist
 
-from ._lib import Experts, Shared, check, lib, ptr, require_cuda, stream_handle
+from ._lib import PATHS, Experts, Shared, check, lib, ptr, require_cuda, stream_handle
 
 
 class ExpertParallel:
@@ -60,9 +60,10 @@ class ExpertParallel:
         p["E_total"] = E
         return p
 
-    def layer(self, p, x, idx, w, limit, capacity=None, out=None):
+    def layer(self, p, x, idx, w, limit, capacity=None, out=None, path="auto"):
         """x bf16 [N_local, H], idx int32 [N_local, k] (global expert ids), w fp32 [N_local, k] -> bf16 [N_local, H].
-        `capacity` = rows per peer in each direction (default N_local * k: never drops)."""
+        `capacity` = rows per peer in each direction (default N_local * k: never drops); `path` = kernels for the
+        received rows ("auto", "decode", "grouped")."""
         require_cuda(x, idx, w)
         N, k = idx.shape
         cap = max(1, capacity if capacity is not None else N * k)
@@ -71,7 +72,8 @@ class ExpertParallel:
         s = p["shared"]
         sh = Shared(s["gate_up_q"].data_ptr(), s["gate_s"].data_ptr(), s["up_s"].data_ptr(), s["down_q"].data_ptr(),
                     s["down_s"].data_ptr(), s["scale_axis"])
-        nbytes = lib().cbmoe_ep_workspace_bytes(ex, N, k, self.nranks, cap)
+        code = PATHS[path]
+        nbytes = lib().cbmoe_ep_workspace_bytes(ex, N, k, self.nranks, cap, code)
         if self._ws is None or self._ws.numel() < nbytes:
             self._ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
         if out is None:
@@ -79,6 +81,7 @@ class ExpertParallel:
         xb = x.to(torch.bfloat16).contiguous()
         check(lib().cbmoe_ep_layer(self.comm, self.nranks, self.rank, ex, p["E_total"], sh, ptr(xb), N,
                                    ptr(idx.to(torch.int32).contiguous()), ptr(w.to(torch.float32).contiguous()), k,
-                                   float(limit), cap, ptr(out), ptr(self._ws), self._ws.numel(), stream_handle()),
+                                   float(limit), cap, code, ptr(out), ptr(self._ws), self._ws.numel(),
+                                   stream_handle()),
               "cbmoe_ep_layer")
         return out

@@ -64,8 +64,6 @@ DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k, long long sl
   w.tail_dn = decode_tail_items((long long)w.P * w.RB_dn);
   w.tail_sgu = decode_tail_items((long long)w.Ps * w.RB_gu);
   w.tail_sdn = decode_tail_items((long long)w.Ps * w.RB_dn);
-  if (w.tail_sgu > kSideCtas / 2) w.tail_sgu = kSideCtas / 2;
-  if (w.tail_sdn > kSideCtas / 2) w.tail_sdn = kSideCtas / 2;
   w.n_zero_routed = 2 + w.P * (w.RB_gu + w.RB_dn);
   w.n_zero_shared = 2 + w.Ps * (w.RB_gu + w.RB_dn);
   w.plan = 0;
@@ -176,7 +174,7 @@ int routed_decode(const cbmoe_experts* ex, const uint16_t* x, int N, const int32
 }
 
 int shared_side(const cbmoe_shared* sh, const uint16_t* x, int N, int H, int I, float limit, uint8_t* ws,
-                const DecodeWorkspace& W, SideStream* side, cudaStream_t stream) {
+                const DecodeWorkspace& W, SideStream* side, cudaStream_t stream, int grid_cap) {
   CBMOE_CUDA_TRY(cudaEventRecord(side->fork, stream));
   CBMOE_CUDA_TRY(cudaStreamWaitEvent(side->s, side->fork, 0));
   int* done_sh = reinterpret_cast<int*>(ws + W.done) + W.n_zero_routed;
@@ -226,7 +224,7 @@ int shared_side(const cbmoe_shared* sh, const uint16_t* x, int N, int H, int I, 
   p.N = N;
   p.limit = limit;
   p.h_out = hs;
-  p.grid_cap = kSideCtas;
+  p.grid_cap = grid_cap;
   p.sched = done_sh;
   p.tail_items = W.tail_sgu;
   p.done = done_sh + 2;
@@ -246,7 +244,7 @@ int shared_side(const cbmoe_shared* sh, const uint16_t* x, int N, int H, int I, 
   d.b_hilo = 1;
   d.N = N;
   d.y_out = reinterpret_cast<float*>(ws + W.ys);
-  d.grid_cap = kSideCtas;
+  d.grid_cap = grid_cap;
   d.sched = done_sh + 1;
   d.tail_items = W.tail_sdn;
   d.done = done_sh + 2 + W.Ps * W.RB_gu;

@@ -96,7 +96,7 @@ struct EpWorkspace {
   lyr::GroupedWorkspace Gr;    // received rows, grouped path
 };
 
-EpWorkspace ep_workspace(int E_loc, int H, int I, int N_local, int k, int nranks, int cap) {
+EpWorkspace ep_workspace(int E_loc, int H, int I, int N_local, int k, int nranks, int cap, int path) {
   using lyr::align_up;
   EpWorkspace w;
   w.R = nranks * cap;
@@ -112,10 +112,17 @@ EpWorkspace ep_workspace(int E_loc, int H, int I, int N_local, int k, int nranks
   w.Wl = lyr::decode_workspace(E_loc, H, I, N_local, k);
   w.sub_recv = w.sub_local + align_up(w.Wl.total);
   // The receive buffer holds up to R rows, but a rank expects about its own slot count (N_local * k) of real
-  // ones: the kernels are chosen by that, tensor-core GEMMs from 8 rows per local expert on.
+  // ones: AUTO chooses the kernels by that, tensor-core GEMMs from 8 rows per local expert on (measured at 1-8
+  // ranks of the config-4 stack: faster than the decode kernels there even with few (expert, tile) items).
   const long long expect = (long long)N_local * k;
-  w.recv_path = (expect >= 8LL * E_loc && H % kGrpTileM == 0 && I % kGrpTileM == 0) ? CBMOE_PATH_GROUPED
-                                                                                   : CBMOE_PATH_DECODE;
+  const bool grouped_ok = H % kGrpTileM == 0 && I % kGrpTileM == 0;
+  if (path == CBMOE_PATH_GROUPED && grouped_ok) {
+    w.recv_path = CBMOE_PATH_GROUPED;
+  } else if (path == CBMOE_PATH_DECODE || !grouped_ok) {
+    w.recv_path = CBMOE_PATH_DECODE;
+  } else {
+    w.recv_path = expect >= 8LL * E_loc ? CBMOE_PATH_GROUPED : CBMOE_PATH_DECODE;
+  }
   size_t rb = 0;
   if (w.recv_path == CBMOE_PATH_GROUPED) {
     w.Gr = lyr::grouped_workspace(E_loc, H, I, w.R, 1);
@@ -186,22 +193,25 @@ extern "C" int cbmoe_ep_comm_destroy(void* comm) {
   return ncclCommDestroy(static_cast<ncclComm_t>(comm)) == ncclSuccess ? CBMOE_OK : CBMOE_ERR_NCCL;
 }
 
-extern "C" size_t cbmoe_ep_workspace_bytes(const cbmoe_experts* local, int N_local, int k, int nranks, int capacity) {
+extern "C" size_t cbmoe_ep_workspace_bytes(const cbmoe_experts* local, int N_local, int k, int nranks, int capacity,
+                                           int path) {
   if (!local || local->E <= 0 || N_local < 0 || k <= 0 || nranks < 1 || capacity <= 0) return 0;
-  return ep_workspace(local->E, local->H, local->I, N_local, k, nranks, capacity).total;
+  if (path != CBMOE_PATH_AUTO && path != CBMOE_PATH_DECODE && path != CBMOE_PATH_GROUPED) return 0;
+  return ep_workspace(local->E, local->H, local->I, N_local, k, nranks, capacity, path).total;
 }
 
 extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_experts* local, int E_total,
                               const cbmoe_shared* sh, const uint16_t* x, int N_local, const int32_t* idx,
-                              const float* w, int k, float limit, int capacity, uint16_t* out, void* workspace,
-                              size_t workspace_bytes, cudaStream_t stream) {
+                              const float* w, int k, float limit, int capacity, int path, uint16_t* out,
+                              void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (!ep_args_ok(comm_v, nranks, rank, local, E_total, N_local, k, capacity) || !lyr::shared_ok(sh))
     return CBMOE_ERR_INVALID;
+  if (path != CBMOE_PATH_AUTO && path != CBMOE_PATH_DECODE && path != CBMOE_PATH_GROUPED) return CBMOE_ERR_INVALID;
   if (N_local > 0 && (!x || !idx || !w || !out || !lyr::aligned16(x) || !lyr::aligned16(out)))
     return CBMOE_ERR_INVALID;
   ncclComm_t comm = static_cast<ncclComm_t>(comm_v);
   const int E_loc = local->E, H = local->H, I = local->I;
-  const EpWorkspace W = ep_workspace(E_loc, H, I, N_local, k, nranks, capacity);
+  const EpWorkspace W = ep_workspace(E_loc, H, I, N_local, k, nranks, capacity, path);
   if (!workspace || workspace_bytes < W.total) return CBMOE_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint16_t* send_x = reinterpret_cast<uint16_t*>(ws + W.send_x);
@@ -217,7 +227,9 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
   const int S = N_local * k;
   int rc = CBMOE_OK;
 
-  // shared expert of the local tokens on the side stream (gate/up, down -> ys)
+  // shared expert of the local tokens on the side stream (gate/up, down -> ys), beside the dispatch and the local
+  // experts; joined before the final combine. (Measured: joining it before the local experts, with the decode
+  // kernels on the whole GPU, is slower at 32-64 tokens per rank: those kernels outlast the dispatch.)
   lyr::SideStream* side = nullptr;
   rc = lyr::side_stream(&side);
   if (rc) return rc;
@@ -248,13 +260,14 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
   if (!rc) rc = exchange(comm, nranks, rank, send_meta, recv_meta, (size_t)capacity, ncclInt32, 4, stream);
   prof_end(kProfExchange, stream);
   if (rc) goto join;
-  // 4. local experts on the received rows (one slot per row, weight 1)
+  // 4. local experts on the received rows (one slot per row, weight 1); the grouped kernels' slot outputs are
+  // bf16, and go back as bf16
   if (W.recv_path == CBMOE_PATH_GROUPED) {
     rc = lyr::routed_grouped(local, recv_x, W.R, recv_meta, ones, 1, limit, wr, W.Gr, stream);
     if (!rc) {
       const int32_t* plan = reinterpret_cast<const int32_t*>(wr + W.Gr.plan);
       rc = launch_combine_bf16(reinterpret_cast<const uint16_t*>(wr + W.Gr.y), plan + W.Gr.L.off[9], ones, W.R, 1, H,
-                               nullptr, y_recv, nullptr, stream);
+                               nullptr, nullptr, reinterpret_cast<uint16_t*>(y_recv), stream);
     }
   } else {
     rc = lyr::routed_decode(local, recv_x, W.R, recv_meta, ones, 1, limit, wr, W.Wr, stream);
@@ -267,12 +280,18 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
   if (rc) goto join;
   // 5. return the expert outputs
   prof_begin(kProfExchange, stream);
-  rc = exchange(comm, nranks, rank, y_recv, y_back, (size_t)capacity * H, ncclFloat32, 4, stream);
+  if (W.recv_path == CBMOE_PATH_GROUPED)
+    rc = exchange(comm, nranks, rank, y_recv, y_back, (size_t)capacity * H, ncclBfloat16, 2, stream);
+  else
+    rc = exchange(comm, nranks, rank, y_recv, y_back, (size_t)capacity * H, ncclFloat32, 4, stream);
   prof_end(kProfExchange, stream);
 join:
   if (N_local > 0) CBMOE_CUDA_TRY(cudaStreamWaitEvent(stream, side->join, 0));
   if (rc || N_local == 0) return rc;
   // 6. weighted sum of the returned rows + the shared expert
-  return launch_combine(y_back, slot_pos, w, N_local, k, H, reinterpret_cast<const float*>(wl + W.Wl.ys), nullptr,
-                        out, stream);
+  const float* ys = reinterpret_cast<const float*>(wl + W.Wl.ys);
+  if (W.recv_path == CBMOE_PATH_GROUPED)
+    return launch_combine_bf16(reinterpret_cast<const uint16_t*>(y_back), slot_pos, w, N_local, k, H, nullptr, nullptr,
+                               out, stream, ys);
+  return launch_combine(y_back, slot_pos, w, N_local, k, H, ys, nullptr, out, stream);
 }

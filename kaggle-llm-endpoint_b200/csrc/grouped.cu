@@ -458,8 +458,8 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
 
 __global__ void combine_bf16_kernel(const uint16_t* __restrict__ y_sorted, const int* __restrict__ row_slot,
                                     const float* __restrict__ wts, int N, int topk, int H,
-                                    const uint16_t* __restrict__ add, float* __restrict__ out_f32,
-                                    uint16_t* __restrict__ out_bf16) {
+                                    const uint16_t* __restrict__ add, const float* __restrict__ add_f32,
+                                    float* __restrict__ out_f32, uint16_t* __restrict__ out_bf16) {
   const int H8 = H / 8;
   const long long total = (long long)N * H8;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -492,6 +492,12 @@ __global__ void combine_bf16_kernel(const uint16_t* __restrict__ y_sorted, const
       bf16x8_to_f32(reinterpret_cast<const uint4*>(add + (size_t)n * H)[c8], f);
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[e] += f[e];
+    }
+    if (add_f32 != nullptr) {
+      const float4* a = reinterpret_cast<const float4*>(add_f32 + (size_t)n * H + (size_t)c8 * 8);
+      const float4 a0 = a[0], a1 = a[1];
+      v[0] += a0.x; v[1] += a0.y; v[2] += a0.z; v[3] += a0.w;
+      v[4] += a1.x; v[5] += a1.y; v[6] += a1.z; v[7] += a1.w;
     }
     const size_t o = (size_t)n * H + (size_t)c8 * 8;
     if (out_f32 != nullptr) {
@@ -539,10 +545,11 @@ int launch_gather_rows(const uint16_t* x, int H, const int* tok_row, int rows, u
 }
 
 int launch_combine_bf16(const uint16_t* y_sorted, const int* row_slot, const float* wts, int N, int topk, int H,
-                        const uint16_t* add_bf16, float* out_f32, uint16_t* out_bf16, cudaStream_t s) {
+                        const uint16_t* add_bf16, float* out_f32, uint16_t* out_bf16, cudaStream_t s,
+                        const float* add_f32) {
   prof_begin(kProfCombine, s);
-  combine_bf16_kernel<<<grid_of((long long)N * H / 8), 256, 0, s>>>(y_sorted, row_slot, wts, N, topk, H, add_bf16, out_f32,
-                                                                 out_bf16);
+  combine_bf16_kernel<<<grid_of((long long)N * H / 8), 256, 0, s>>>(y_sorted, row_slot, wts, N, topk, H, add_bf16,
+                                                                 add_f32, out_f32, out_bf16);
   prof_end(kProfCombine, s);
   CBMOE_CUDA_TRY(cudaGetLastError());
   return CBMOE_OK;

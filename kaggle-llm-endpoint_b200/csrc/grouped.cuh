@@ -37,6 +37,7 @@ int grouped_w8_store(const GroupedParams& p, const void* b, int b_rows, cudaStre
 int grouped_w8_store_f32(const GroupedParams& p, const void* b, int b_rows, cudaStream_t s);
 int launch_gather_rows(const uint16_t* x, int H, const int* tok_row, int rows, uint16_t* xs, cudaStream_t s);
 int launch_combine_bf16(const uint16_t* y_sorted, const int* row_slot, const float* wts, int N, int topk, int H,
-                        const uint16_t* add_bf16, float* out_f32, uint16_t* out_bf16, cudaStream_t s);
+                        const uint16_t* add_bf16, float* out_f32, uint16_t* out_bf16, cudaStream_t s,
+                        const float* add_f32 = nullptr);
 
 }  // namespace cbmoe

@@ -47,8 +47,9 @@ constexpr int kW8DecodeMaxTokens = 64;
 // Shared expert of one layer call on the side stream (forked after the caller's prior work on `stream`, its
 // counters zeroed there first): gate/up (x -> hs, SwiGLU) then down (hs -> ys f32), by the decode kernels up to
 // kW8DecodeMaxTokens tokens and the tensor-core kernels above. The caller joins `side->join` before reading ys.
+// grid_cap: CTAs of the decode kernels (kSideCtas beside routed kernels; 0: the whole GPU).
 int shared_side(const cbmoe_shared* sh, const uint16_t* x, int N, int H, int I, float limit, uint8_t* ws,
-                const DecodeWorkspace& W, SideStream* side, cudaStream_t stream);
+                const DecodeWorkspace& W, SideStream* side, cudaStream_t stream, int grid_cap = kSideCtas);
 
 size_t align_up(size_t v);
 PlanLayoutHost host_plan_layout(int T, int k, int E, int tm, int pass_tokens);

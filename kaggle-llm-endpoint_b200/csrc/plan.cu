@@ -273,19 +273,31 @@ __global__ void __launch_bounds__(kPlanThreads) plan_scan_kernel(int T, int k, i
   extern __shared__ int sm[];
   int* counts = sm;        // [E]
   int* ends = sm + E;      // [E]
+  int* bases = sm + 2 * E; // [E] first sorted row of each expert
   __shared__ int s_tot[4];
   __shared__ int s_chunk[4][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < n_zero; i += kPlanThreads) zero[i] = 0;
-  // per-expert totals; chunk counts -> exclusive prefix over chunks (relative to the expert's first row)
-  for (int e = threadIdx.x; e < E; e += kPlanThreads) {
-    int run = 0;
-    for (int c = 0; c < n_chunks; ++c) {
-      const int v = chunk_cnt[c * E + e];
-      chunk_cnt[c * E + e] = run;
-      run += v;
+  // per-expert totals; chunk counts -> exclusive prefix over chunks (relative to the expert's first row). One warp
+  // per expert, one chunk per lane: the loads are issued together instead of as a chain of dependent round trips.
+  constexpr int kMaxGroups = (kPlanMaxChunks + 31) / 32;
+  for (int e = warp; e < E; e += kPlanWarps) {
+    int v[kMaxGroups];
+#pragma unroll
+    for (int gi = 0; gi < kMaxGroups; ++gi) {
+      const int c = gi * 32 + lane;
+      v[gi] = c < n_chunks ? chunk_cnt[c * E + e] : 0;
     }
-    counts[e] = run;
+    int carry = 0;
+#pragma unroll
+    for (int gi = 0; gi < kMaxGroups; ++gi) {
+      const int c = gi * 32 + lane;
+      int tot;
+      const int ex = warp_exclusive_scan(v[gi], &tot);
+      if (c < n_chunks) chunk_cnt[c * E + e] = carry + ex;
+      carry += tot;
+    }
+    if (lane == 0) counts[e] = carry;
   }
   __syncthreads();
   int32_t* counts_g = plan + L.off[0];
@@ -342,8 +354,14 @@ __global__ void __launch_bounds__(kPlanThreads) plan_scan_kernel(int T, int k, i
         pass_row0[x_pass + p] = x_rows + p * pass_tokens;
         pass_cnt[x_pass + p] = min(pass_tokens, c - p * pass_tokens);
       }
-      for (int cc = 0; cc < n_chunks; ++cc) chunk_cnt[cc * E + e] += x_rows;   // absolute chunk bases
     }
+    if (e < E) bases[e] = x_rows;
+  }
+  __syncthreads();
+  // absolute chunk bases: one warp per expert, one chunk per lane
+  for (int e = warp; e < E; e += kPlanWarps) {
+    const int base = bases[e];
+    for (int c = lane; c < n_chunks; c += 32) chunk_cnt[c * E + e] += base;
   }
   if (threadIdx.x == 0) {
     s_tot[0] = tot_act;
@@ -451,7 +469,7 @@ int launch_route_plan(const int32_t* idx, const float* w, int T, int k, int E, i
     const size_t csmem = (size_t)kPlanCtaWarps * E * 4;
     prof_begin(kProfPlan, stream);
     plan_count_kernel<<<n_chunks, kPlanCtaWarps * 32, csmem, stream>>>(idx, (int)S, E, chunk);
-    plan_scan_kernel<<<1, kPlanThreads, 2 * E * 4, stream>>>(T, k, E, tm, pass_tokens, n_chunks, plan, L, chunk, zero,
+    plan_scan_kernel<<<1, kPlanThreads, 3 * E * 4, stream>>>(T, k, E, tm, pass_tokens, n_chunks, plan, L, chunk, zero,
                                                              n_zero);
     plan_place_kernel<<<n_chunks, kPlanCtaWarps * 32, csmem, stream>>>(idx, w, (int)S, k, E, plan, L, chunk);
     prof_end(kProfPlan, stream);

@@ -54,17 +54,26 @@ def cb3_table(rng, n_experts, rows, K):
     return cb3.pack(q), cb3.make_codebooks(rng, (n_experts, rows))
 
 
+def cb3_table_words(rng, n_experts, rows, K):
+    """The same distribution as cb3_table, drawn as random words: every bit of a CB3 bit stream is an independent
+    fair bit, so uniform uint32 words are uniform 3-bit indices. Fast enough for full-size layers."""
+    words = rng.integers(0, 2 ** 32, size=(n_experts, rows, cb3.words_per_row(K)), dtype=np.uint32)
+    return words, cb3.make_codebooks(rng, (n_experts, rows))
+
+
 def q8_leaf(rng, n_in, n_out, axis=1, std=0.02):
     """int8 leaf (q [in, out], s) quantized from an N(0, std) matrix as quant8.quantize_array does."""
     w = rng.standard_normal((n_in, n_out)).astype(np.float32) * np.float32(std)
     return q8.quantize_array(w, axis)
 
 
-def moe_layer(rng, n_experts=E, hidden=H, inter=I, shared_axis=1):
-    """Routed CB3 tables and int8 shared expert for one layer: dict(gate, up, down, shared=(gate, up, down))."""
-    gate = cb3_table(rng, n_experts, inter, hidden)
-    up = cb3_table(rng, n_experts, inter, hidden)
-    down = cb3_table(rng, n_experts, hidden, inter)
+def moe_layer(rng, n_experts=E, hidden=H, inter=I, shared_axis=1, words=False):
+    """Routed CB3 tables and int8 shared expert for one layer: dict(gate, up, down, shared=(gate, up, down)).
+    words=True draws the index bits as random words (cb3_table_words) instead of packing drawn indices."""
+    table = cb3_table_words if words else cb3_table
+    gate = table(rng, n_experts, inter, hidden)
+    up = table(rng, n_experts, inter, hidden)
+    down = table(rng, n_experts, hidden, inter)
     shared = (q8_leaf(rng, hidden, inter, shared_axis), q8_leaf(rng, hidden, inter, shared_axis),
               q8_leaf(rng, inter, hidden, shared_axis))
     return {"gate": gate, "up": up, "down": down, "shared": shared}

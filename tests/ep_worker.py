@@ -32,7 +32,8 @@ def main():
         E, H, I, k = 8, 512, 256, 4
         rng = np.random.default_rng(123)
         L = gen.moe_layer(rng, E, H, I)
-        for case, (N_total, cap) in enumerate([(16, None), (64, None), (6, 3)]):
+        for case, (N_total, cap, path) in enumerate([(16, None, "auto"), (64, None, "auto"), (64, None, "grouped"),
+                                                      (6, 3, "auto")]):
             x = gen.activations(rng, N_total, H)
             idx, w = gen.routing(rng, N_total, E, k)
             per = N_total // world
@@ -40,7 +41,7 @@ def main():
             p = group.pack_local(table_to_gpu(L["gate"]), table_to_gpu(L["up"]), table_to_gpu(L["down"]),
                                  shared_to_gpu(L["shared"]))
             out = group.layer(p, t_bf16(x[sl]), torch.from_numpy(idx[sl]).cuda(), torch.from_numpy(w[sl]).cuda(),
-                              gen.LIMIT, capacity=cap)
+                              gen.LIMIT, capacity=cap, path=path)
             torch.cuda.synchronize()
             errs = cbmoe.device_errors(clear=True)
             outs = [torch.empty_like(out) for _ in range(world)]
@@ -51,7 +52,8 @@ def main():
                                      L["gate"], L["up"], L["down"], L["shared"], gen.LIMIT)
                 err = moe.max_rel_err(got, want)
                 dropped = errs & 4
-                print(f"case {case}: N={N_total} cap={cap} max rel err {err:.2e} device errors {errs}", flush=True)
+                print(f"case {case}: N={N_total} cap={cap} path={path} max rel err {err:.2e} device errors {errs}",
+                      flush=True)
                 if cap is None:
                     ok = ok and err < 1e-2 and errs == 0
                 else:
