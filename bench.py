@@ -18,7 +18,8 @@ every step; roofline = the dominant kernel's algorithmic bytes / its event-timed
 peak; cpu_baseline = the C oracle (OpenMP) on a bounded sample of the same workload on this host's cores.
 --impl reference times that CPU restatement alone (the reference's own path is JAX-on-TPU and cannot run here).
 N > 1: expert parallelism, config 1 per GPU: each rank owns 8 tokens and E/N of the 160 experts of every layer;
-a step routes all ranks' slots to the ranks holding their experts (NCCL send/recv), computes, returns and combines
+a step routes all ranks' slots to the ranks holding their experts (written straight into their memory over NVLink;
+--ep-transport nccl: NCCL send/recv), computes, returns and combines
 (scaling "weak": 8 tokens per GPU at every N; `value` = all ranks' tokens / the slowest rank's time).
 """
 import argparse
@@ -60,19 +61,22 @@ def parse():
     ap.add_argument("--workload", choices=["decode", "prefill", "ep"], default="decode",
                     help="decode = config 1 (the default bench line); prefill = config 3 (4096 tokens, tcgen05 path); "
                          "ep = config 4 (4 layers, 256 tokens, experts sharded over the GPUs, strong scaling)")
+    ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: dispatch/return through peer memory over NVLink, or NCCL send/recv")
     ap.add_argument("--ep-path", choices=["auto", "decode", "grouped"], default="auto",
                     help="expert kernels of --workload ep (N > 1: for the rows each rank receives)")
     return ap.parse_args()
 
 
-def config_block(n_gpus):
+def config_block(n_gpus, transport=None):
     return {"workload": "config1: MoE decode layer, 8 tokens, E=160 CB3 routed + int8 shared, H=5120, I=1536, top-8",
             "global_batch": N_TOK * n_gpus, "tokens_per_gpu": N_TOK, "hidden": H, "experts": E, "intermediate": I,
             "topk": TOPK, "expert_format": "CB3 (3-bit indices, 8-entry bf16 codebook per row)",
             "shared_format": "int8 per-output-channel, fp32 scales",
             "l2": "inputs larger than L2: 16 resident layers (1.47 GB each) cycled, ~0.5 GB of fresh weights per step",
-            "parallelism": f"expert parallel x{n_gpus} (NCCL dispatch/combine, 8 tokens per GPU)" if n_gpus > 1
-            else "single GPU"}
+            "parallelism": f"expert parallel x{n_gpus} (dispatch/return over NVLink, 8 tokens per GPU)" if n_gpus > 1
+            else "single GPU",
+            "transport": transport if n_gpus > 1 else None}
 
 
 # ------------------------------------------------------------------------------------------------ clocks
@@ -287,7 +291,7 @@ def run_reference(args):
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / len(times),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": config_block(args.gpus),
+            "config": config_block(args.gpus, args.ep_transport),
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "reference path is JAX/Pallas for TPU (JAX absent here): timed arm is the oracle's C port"}
@@ -340,7 +344,7 @@ def run_ours(args):
     if world > 1:
         # expert parallel: every rank generates each layer from the same seed and keeps its E/world experts
         from cbmoe.ep import ExpertParallel
-        group = ExpertParallel()
+        group = ExpertParallel(transport=args.ep_transport)
         for li in range(n_layers):
             full, std = make_layer_tables(torch, 1000 + li, dev)
             layers.append(group.pack_local(*full))
@@ -490,7 +494,7 @@ def run_ours(args):
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": config_block(world), "clocks": clocks.summary(), "gpu_launches": launches,
+                "config": config_block(world, args.ep_transport), "clocks": clocks.summary(), "gpu_launches": launches,
                 "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "ms_per_step": ms_e2e / args.steps},
                 "roofline": roofline,
@@ -669,7 +673,7 @@ T_EP, L_EP = 256, 4
 
 def run_ep_stack(args):
     """Config 4: 4 MoE layers of the config-1 shape on 256 tokens (uniform top-8), the 160 experts sharded over the
-    N GPUs (expert parallelism, NCCL dispatch and return); every rank holds 256/N of the tokens. Strong scaling: the
+    N GPUs (expert parallelism, dispatch and return over NVLink); every rank holds 256/N of the tokens. Strong scaling: the
     global batch is the same at every N. N = 1 runs the same 4 layers through the single-GPU layer call."""
     import torch
     import torch.distributed as dist
@@ -690,7 +694,7 @@ def run_ep_stack(args):
     layers = []
     if world > 1:
         from cbmoe.ep import ExpertParallel
-        group = ExpertParallel()
+        group = ExpertParallel(transport=args.ep_transport)
         for li in range(L_EP):
             full, _ = make_layer_tables(torch, 3000 + li, dev)
             layers.append(group.pack_local(*full))
@@ -801,7 +805,8 @@ def run_ep_stack(args):
                                        "160 CB3 experts sharded over the GPUs + replicated int8 shared expert",
                            "global_batch": T_EP, "tokens_per_gpu": t_loc, "layers": L_EP,
                            "experts_per_gpu": E // world, "capacity_rows_per_peer": cap if world > 1 else None,
-                           "path": path, "parallelism": f"expert parallel x{world}" if world > 1 else "single GPU",
+                           "path": path, "transport": args.ep_transport if world > 1 else None,
+                           "parallelism": f"expert parallel x{world}" if world > 1 else "single GPU",
                            "l2": "4 resident layers (1.47 GB each) per step: inputs larger than L2"},
                 "clocks": clocks.summary(), "gpu_launches": launches,
                 "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d * world,

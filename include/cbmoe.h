@@ -179,8 +179,15 @@ size_t cbmoe_ep_workspace_bytes(const cbmoe_experts* local, int N_local, int k, 
  * expected rows per local expert, N_local * k >= 8 * local->E). */
 int cbmoe_ep_layer(void* comm, int nranks, int rank, const cbmoe_experts* local, int E_total, const cbmoe_shared* sh,
                    const uint16_t* x, int N_local, const int32_t* idx, const float* w, int k, float limit,
-                   int capacity, int path, uint16_t* out, void* workspace, size_t workspace_bytes,
+                   int capacity, int path, void* peer, uint16_t* out, void* workspace, size_t workspace_bytes,
                    cudaStream_t stream);
+/* Peer-memory transport for cbmoe_ep_layer (peer != NULL there): the dispatch and the return are written straight
+ * into the other GPUs' memory over NVLink (CUDA IPC mappings) instead of NCCL send/recv; every wait on a peer is
+ * bounded (CBMOE_DEVERR_TIMEOUT). Collective: every rank calls cbmoe_ep_peer_init with the same H and capacity
+ * (nranks <= 8, one process per GPU of one node); cbmoe_ep_layer then requires that capacity. Destroy after all
+ * ranks are past their last layer call (e.g. after a barrier). */
+int cbmoe_ep_peer_init(void* comm, int nranks, int rank, int H, int capacity, cudaStream_t stream, void** peer_out);
+int cbmoe_ep_peer_destroy(void* peer);
 
 #ifdef __cplusplus
 }

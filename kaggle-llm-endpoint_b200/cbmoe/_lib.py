@@ -63,7 +63,9 @@ SIGNATURES = {
     "cbmoe_ep_workspace_bytes": (c_size_t, [ctypes.POINTER(Experts), c_int, c_int, c_int, c_int, c_int]),
     "cbmoe_ep_layer": (c_int, [c_void_p, c_int, c_int, ctypes.POINTER(Experts), c_int, ctypes.POINTER(Shared),
                                c_void_p, c_int, c_void_p, c_void_p, c_int, c_float, c_int, c_int, c_void_p,
-                               c_void_p, c_size_t, c_void_p]),
+                               c_void_p, c_void_p, c_size_t, c_void_p]),
+    "cbmoe_ep_peer_init": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, ctypes.POINTER(c_void_p)]),
+    "cbmoe_ep_peer_destroy": (c_int, [c_void_p]),
     "cbmoe_cb3_matvec": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_size_t,
                                  c_void_p]),
     "cbmoe_w8_linear": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p,

@@ -19,7 +19,10 @@ from ._lib import PATHS, Experts, Shared, check, lib, ptr, require_cuda, stream_
 
 
 class ExpertParallel:
-    def __init__(self, group=None):
+    """`transport`: "peer" (dispatch and return written straight into the other GPUs' memory over NVLink, CUDA IPC
+    buffers set up on the first layer call, one process per GPU of one node, at most 8) or "nccl" (send/recv)."""
+
+    def __init__(self, group=None, transport="peer"):
         self.rank = dist.get_rank(group)
         self.nranks = dist.get_world_size(group)
         idbuf = torch.zeros(128, dtype=torch.uint8)
@@ -39,8 +42,32 @@ class ExpertParallel:
         check(lib().cbmoe_ep_comm_init(raw, self.nranks, self.rank, ctypes.byref(comm)), "cbmoe_ep_comm_init")
         self.comm = comm
         self._ws = None
+        assert transport in ("peer", "nccl"), transport
+        self.transport = transport if self.nranks <= 8 else "nccl"
+        self._peer, self._peer_key = None, None
+
+    def _peer_for(self, H, cap):
+        """The peer-memory buffers for (H, cap); collective: every rank reaches it in the same layer call."""
+        if self.transport != "peer":
+            return None
+        if self._peer_key != (H, cap):
+            if self._peer is not None:
+                torch.cuda.synchronize()
+                check(lib().cbmoe_ep_peer_destroy(self._peer), "cbmoe_ep_peer_destroy")
+                self._peer = None
+            peer = ctypes.c_void_p()
+            check(lib().cbmoe_ep_peer_init(self.comm, self.nranks, self.rank, H, cap, stream_handle(),
+                                           ctypes.byref(peer)), "cbmoe_ep_peer_init")
+            self._peer, self._peer_key = peer, (H, cap)
+        return self._peer
 
     def close(self):
+        if self._peer is not None:
+            torch.cuda.synchronize()
+            if dist.is_initialized():
+                dist.barrier()   # every rank is past its last layer call before the buffers go
+            check(lib().cbmoe_ep_peer_destroy(self._peer), "cbmoe_ep_peer_destroy")
+            self._peer = None
         if self.comm:
             check(lib().cbmoe_ep_comm_destroy(self.comm), "cbmoe_ep_comm_destroy")
             self.comm = None
@@ -79,9 +106,10 @@ class ExpertParallel:
         if out is None:
             out = torch.empty((N, p["H"]), dtype=torch.bfloat16, device=x.device)
         xb = x.to(torch.bfloat16).contiguous()
+        peer = self._peer_for(p["H"], cap)
         check(lib().cbmoe_ep_layer(self.comm, self.nranks, self.rank, ex, p["E_total"], sh, ptr(xb), N,
                                    ptr(idx.to(torch.int32).contiguous()), ptr(w.to(torch.float32).contiguous()), k,
-                                   float(limit), cap, code, ptr(out), ptr(self._ws), self._ws.numel(),
+                                   float(limit), cap, code, peer, ptr(out), ptr(self._ws), self._ws.numel(),
                                    stream_handle()),
               "cbmoe_ep_layer")
         return out

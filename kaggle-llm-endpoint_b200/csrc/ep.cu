@@ -202,8 +202,8 @@ extern "C" size_t cbmoe_ep_workspace_bytes(const cbmoe_experts* local, int N_loc
 
 extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_experts* local, int E_total,
                               const cbmoe_shared* sh, const uint16_t* x, int N_local, const int32_t* idx,
-                              const float* w, int k, float limit, int capacity, int path, uint16_t* out,
-                              void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+                              const float* w, int k, float limit, int capacity, int path, void* peer_v,
+                              uint16_t* out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (!ep_args_ok(comm_v, nranks, rank, local, E_total, N_local, k, capacity) || !lyr::shared_ok(sh))
     return CBMOE_ERR_INVALID;
   if (path != CBMOE_PATH_AUTO && path != CBMOE_PATH_DECODE && path != CBMOE_PATH_GROUPED) return CBMOE_ERR_INVALID;
@@ -211,17 +211,19 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
     return CBMOE_ERR_INVALID;
   ncclComm_t comm = static_cast<ncclComm_t>(comm_v);
   const int E_loc = local->E, H = local->H, I = local->I;
+  EpPeer* pe = static_cast<EpPeer*>(peer_v);
+  if (pe && !ep_peer_matches(pe, nranks, rank, H, capacity)) return CBMOE_ERR_INVALID;
   const EpWorkspace W = ep_workspace(E_loc, H, I, N_local, k, nranks, capacity, path);
   if (!workspace || workspace_bytes < W.total) return CBMOE_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint16_t* send_x = reinterpret_cast<uint16_t*>(ws + W.send_x);
-  uint16_t* recv_x = reinterpret_cast<uint16_t*>(ws + W.recv_x);
+  uint16_t* recv_x = pe ? ep_peer_in_x(pe) : reinterpret_cast<uint16_t*>(ws + W.recv_x);
   int32_t* send_meta = reinterpret_cast<int32_t*>(ws + W.send_meta);
-  int32_t* recv_meta = reinterpret_cast<int32_t*>(ws + W.recv_meta);
+  int32_t* recv_meta = pe ? ep_peer_in_meta(pe) : reinterpret_cast<int32_t*>(ws + W.recv_meta);
   int32_t* slot_pos = reinterpret_cast<int32_t*>(ws + W.slot_pos);
   float* ones = reinterpret_cast<float*>(ws + W.ones);
   float* y_recv = reinterpret_cast<float*>(ws + W.y_recv);
-  float* y_back = reinterpret_cast<float*>(ws + W.y_back);
+  float* y_back = pe ? static_cast<float*>(ep_peer_in_y(pe)) : reinterpret_cast<float*>(ws + W.y_back);
   uint8_t* wl = ws + W.sub_local;
   uint8_t* wr = ws + W.sub_recv;
   const int S = N_local * k;
@@ -244,7 +246,11 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
                                                 W.R);
   prof_end(kProfOther, stream);
   CBMOE_CUDA_TRY(cudaGetLastError());
-  if (S > 0) {
+  if (pe) {   // 2-3. rows straight into the destinations' memory
+    rc = ep_peer_dispatch(pe, x, H, slot_pos, S, k, send_meta, stream);
+    if (rc) goto join;
+  }
+  if (S > 0 && !pe) {
     prof_begin(kProfOther, stream);
     const long long total = (long long)S * (H / 8);
     int blocks = (int)((total + 255) / 256);
@@ -255,10 +261,12 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
     CBMOE_CUDA_TRY(cudaGetLastError());
   }
   // 3. dispatch
-  prof_begin(kProfExchange, stream);
-  rc = exchange(comm, nranks, rank, send_x, recv_x, (size_t)capacity * H, ncclBfloat16, 2, stream);
-  if (!rc) rc = exchange(comm, nranks, rank, send_meta, recv_meta, (size_t)capacity, ncclInt32, 4, stream);
-  prof_end(kProfExchange, stream);
+  if (!pe) {
+    prof_begin(kProfExchange, stream);
+    rc = exchange(comm, nranks, rank, send_x, recv_x, (size_t)capacity * H, ncclBfloat16, 2, stream);
+    if (!rc) rc = exchange(comm, nranks, rank, send_meta, recv_meta, (size_t)capacity, ncclInt32, 4, stream);
+    prof_end(kProfExchange, stream);
+  }
   if (rc) goto join;
   // 4. local experts on the received rows (one slot per row, weight 1); the grouped kernels' slot outputs are
   // bf16, and go back as bf16
@@ -266,18 +274,24 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
     rc = lyr::routed_grouped(local, recv_x, W.R, recv_meta, ones, 1, limit, wr, W.Gr, stream);
     if (!rc) {
       const int32_t* plan = reinterpret_cast<const int32_t*>(wr + W.Gr.plan);
-      rc = launch_combine_bf16(reinterpret_cast<const uint16_t*>(wr + W.Gr.y), plan + W.Gr.L.off[9], ones, W.R, 1, H,
-                               nullptr, nullptr, reinterpret_cast<uint16_t*>(y_recv), stream);
+      if (pe)   // 4-5. outputs straight into the sources' memory
+        rc = ep_peer_return(pe, wr + W.Gr.y, true, plan + W.Gr.L.off[9], recv_meta, W.R, H, stream);
+      else
+        rc = launch_combine_bf16(reinterpret_cast<const uint16_t*>(wr + W.Gr.y), plan + W.Gr.L.off[9], ones, W.R, 1,
+                                 H, nullptr, nullptr, reinterpret_cast<uint16_t*>(y_recv), stream);
     }
   } else {
     rc = lyr::routed_decode(local, recv_x, W.R, recv_meta, ones, 1, limit, wr, W.Wr, stream);
     if (!rc) {
       const int32_t* plan = reinterpret_cast<const int32_t*>(wr + W.Wr.plan);
-      rc = launch_combine(reinterpret_cast<const float*>(wr + W.Wr.y), plan + W.Wr.L.off[9], ones, W.R, 1, H,
-                          nullptr, y_recv, nullptr, stream);
+      if (pe)
+        rc = ep_peer_return(pe, wr + W.Wr.y, false, plan + W.Wr.L.off[9], recv_meta, W.R, H, stream);
+      else
+        rc = launch_combine(reinterpret_cast<const float*>(wr + W.Wr.y), plan + W.Wr.L.off[9], ones, W.R, 1, H,
+                            nullptr, y_recv, nullptr, stream);
     }
   }
-  if (rc) goto join;
+  if (rc || pe) goto join;
   // 5. return the expert outputs
   prof_begin(kProfExchange, stream);
   if (W.recv_path == CBMOE_PATH_GROUPED)

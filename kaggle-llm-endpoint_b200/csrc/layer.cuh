@@ -70,4 +70,15 @@ int routed_grouped(const cbmoe_experts* ex, const uint16_t* x, int N, const int3
                    float limit, uint8_t* ws, const GroupedWorkspace& W, cudaStream_t stream);
 
 }  // namespace lyr
+
+// Peer-memory transport of the expert-parallel layer (ep_peer.cu).
+struct EpPeer;
+bool ep_peer_matches(const EpPeer* pe, int nranks, int rank, int H, int cap);
+int ep_peer_dispatch(EpPeer* pe, const uint16_t* x, int H, const int32_t* slot_pos, int S, int k,
+                     const int32_t* send_meta, cudaStream_t stream);
+int ep_peer_return(EpPeer* pe, const void* y_sorted, bool bf16, const int32_t* row_slot, const int32_t* recv_meta,
+                   int R, int H, cudaStream_t stream);
+uint16_t* ep_peer_in_x(EpPeer* pe);
+int32_t* ep_peer_in_meta(EpPeer* pe);
+void* ep_peer_in_y(EpPeer* pe);
 }  // namespace cbmoe

@@ -1,5 +1,6 @@
-"""Expert parallelism on 2 GPUs (NCCL over NVLink) against the single-process oracle: runs tests/ep_worker.py under
-torchrun as child processes. Skipped when fewer than 2 GPUs are visible (-m gpu on a 1-GPU box)."""
+"""Expert parallelism on 2 GPUs (peer memory over NVLink, and NCCL send/recv) against the single-process oracle:
+runs tests/ep_worker.py under torchrun as child processes. Skipped when fewer than 2 GPUs are visible (-m gpu on a
+1-GPU box). Every wait on a peer is bounded, so a failure ends the ranks with an error, not a hang."""
 import os
 import socket
 import subprocess
