@@ -37,6 +37,11 @@ extern "C" {
 #define CBMOE_PATH_AUTO 0          /* decode kernel for small batches, grouped tensor-core GEMM otherwise */
 #define CBMOE_PATH_DECODE 1        /* fused dequant matvec (resident.py:110-120 `_apply_kernel`) */
 #define CBMOE_PATH_GROUPED 2       /* grouped dequant GEMM (resident.py:144-165 `_apply_ragged_kernel`) */
+#define CBMOE_PATH_DECODE_TC 3     /* the decode composition with the dequantized weights stored into TMEM and
+                                      contracted by tcgen05.mma (H, I multiples of 128). Same results as
+                                      CBMOE_PATH_DECODE within rounding; slower at every measured size on B200
+                                      (a 128x16x16 tcgen05.mma costs as long as a 128x128x16 one), kept for
+                                      comparison. Not used by CBMOE_PATH_AUTO. */
 
 /* ---------------------------------------------------------------------------------------------- library */
 int cbmoe_version(void);

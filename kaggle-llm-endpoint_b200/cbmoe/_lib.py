@@ -10,7 +10,7 @@ LIB_PATH = os.path.join(_HERE, "libcbmoe.so")
 
 c_int, c_float, c_size_t, c_void_p, c_int64 = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int64
 
-PATHS = {"auto": 0, "decode": 1, "grouped": 2}
+PATHS = {"auto": 0, "decode": 1, "grouped": 2, "decode_tc": 3}
 
 
 class CbmoeError(RuntimeError):

@@ -55,7 +55,7 @@ class ResidentFetch:
     Constructor knobs keep the reference's names: `qtypes` {layer: {"gate_q", "up_q", "down_q"} -> format}
     ("CB3" only here), `D`, `ml` (this GPU's intermediate size), `out_dtype` of the returned partial,
     `gather_max_rows` (slots N*k at or below which the decode kernels run; above it the grouped path), and
-    `path` to force "decode" or "grouped"."""
+    `path` to force "decode", "grouped" or "decode_tc" (the decode composition on the tcgen05 TMEM kernels)."""
 
     def __init__(self, qtypes=None, D=None, ml=None, out_dtype=torch.float32, gather_max_rows=1024, path="auto"):
         self.qtypes = qtypes or {}

@@ -28,20 +28,29 @@ PlanLayoutHost host_plan_layout(int T, int k, int E, int tm, int pass_tokens) {
 // Token tiles (of 8) per pass of the decode kernels. Shared expert: every token goes to the one expert, so by N.
 int decode_nt(int N) { return N <= 8 ? 1 : (N <= 16 ? 2 : 4); }
 // Routed experts: by the average slots per expert (an expert with more tokens than a pass takes several passes;
-// larger passes cost shared memory and occupancy on every item).
+// larger passes cost shared memory, occupancy and MMA issue slots on every item). Measured on one B200 at 12.8
+// slots per expert (20-80 experts): 16-token passes 1.8x faster than 32-token ones, 1.1-1.3x faster than 8-token
+// ones; at 6.4 slots per expert 8-token passes 1.1x faster than 16-token ones, 2.1x than 32-token ones.
 int decode_nt_routed(int N, int k, int E) {
   const long long S = (long long)N * k;
-#ifndef CBMOE_NT2_SLOTS_PER_EXPERT
-#define CBMOE_NT2_SLOTS_PER_EXPERT 6
+#ifndef CBMOE_NT1_SLOTS_PER_EXPERT
+#define CBMOE_NT1_SLOTS_PER_EXPERT 2
 #endif
-  return S <= 2LL * E ? 1 : (S <= (long long)CBMOE_NT2_SLOTS_PER_EXPERT * E ? 2 : 4);
+#ifndef CBMOE_NT2_SLOTS_PER_EXPERT
+#define CBMOE_NT2_SLOTS_PER_EXPERT 16
+#endif
+  return S <= (long long)CBMOE_NT1_SLOTS_PER_EXPERT * E ? 1
+                                                        : (S <= (long long)CBMOE_NT2_SLOTS_PER_EXPERT * E ? 2 : 4);
 }
 
 // Workspace of the decode path:
-//   plan | h (Rp x 2I bf16) | y_sorted (Rp x H f32) | h_shared (N x 2I bf16) | y_shared (N x H f32) |
-//   scheduling words: routed [gate/up tickets, down tickets, gate/up item counters, down item counters]
+//   plan | xs (Rp x H bf16: the routed rows gathered in plan order, CBMOE_PATH_DECODE_TC only) | h (Rp x 2I bf16) |
+//   y_sorted (Rp x H f32) | h_shared (N x 2I bf16) | y_shared (N x H f32) |
+//   scheduling words: routed [gate/up tickets, down tickets, gate/up arrival counters, down arrival counters]
 //                     (zeroed by the plan kernel), shared [the same] (zeroed by a memset on the side stream) |
 //   partial sums of the tail items' pieces of the routed gate/up, routed down, shared gate/up, shared down.
+// h is [row][2I] (hi, lo per 256-input stage) for the mma.sync kernels and two planes [2][Rp][I] (hi, lo) for
+// the tcgen05 ones.
 
 // Tail items a decode launch cuts into pieces: at most half its resident grid (the kernel takes the same bound).
 int decode_tail_items(long long items) {
@@ -49,32 +58,42 @@ int decode_tail_items(long long items) {
   return (int)(items < half ? items : half);
 }
 
-DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k, long long slots_hint) {
+DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k, long long slots_hint, int tc) {
   DecodeWorkspace w;
-  w.nt = slots_hint >= 0 ? decode_nt_routed((int)(slots_hint < N ? slots_hint : N), 1, E) : decode_nt_routed(N, k, E);
+  const long long S_real = slots_hint >= 0 ? (slots_hint < N ? slots_hint : N) : (long long)N * k;
+  w.tc = tc && H % kTcTileM == 0 && I % kTcTileM == 0;
+  w.nt = slots_hint >= 0 ? decode_nt_routed((int)S_real, 1, E) : decode_nt_routed(N, k, E);
+  w.tn = tc_pass_tokens(S_real, E);
   w.nt_s = decode_nt(N);
-  const int pt = 8 * w.nt;
+  const int pt = w.tc ? w.tn : 8 * w.nt;
   w.L = host_plan_layout(N, k, E, 1, pt);
   w.Rp = (int)(w.L.off[8] - w.L.off[7]);
   w.P = (int)(w.L.off[11] - w.L.off[10]);
   w.Ps = (N + 8 * w.nt_s - 1) / (8 * w.nt_s);   // shared-expert passes
   w.RB_gu = I / kRowsPerBlock;
   w.RB_dn = H / kRowsPerBlock;
-  w.tail_gu = decode_tail_items((long long)w.P * w.RB_gu);
-  w.tail_dn = decode_tail_items((long long)w.P * w.RB_dn);
+  if (w.tc) {
+    w.tail_gu = tc_tail_items((long long)w.P * (I / kTcTileM));
+    w.tail_dn = tc_tail_items((long long)w.P * (H / kTcTileM));
+    w.n_zero_routed = 2 + 4 * (w.tail_gu + w.tail_dn);
+  } else {
+    w.tail_gu = decode_tail_items((long long)w.P * w.RB_gu);
+    w.tail_dn = decode_tail_items((long long)w.P * w.RB_dn);
+    w.n_zero_routed = 2 + w.P * (w.RB_gu + w.RB_dn);
+  }
   w.tail_sgu = decode_tail_items((long long)w.Ps * w.RB_gu);
   w.tail_sdn = decode_tail_items((long long)w.Ps * w.RB_dn);
-  w.n_zero_routed = 2 + w.P * (w.RB_gu + w.RB_dn);
   w.n_zero_shared = 2 + w.Ps * (w.RB_gu + w.RB_dn);
   w.plan = 0;
-  w.h = align_up((size_t)w.L.off[13] * 4);
+  w.xs = align_up((size_t)w.L.off[13] * 4);
+  w.h = w.xs + (w.tc ? align_up((size_t)w.Rp * H * 2) : 0);
   w.y = w.h + align_up((size_t)w.Rp * 2 * I * 2);
   w.hs = w.y + align_up((size_t)w.Rp * H * 4);
   w.ys = w.hs + align_up((size_t)N * 2 * I * 2);
   w.done = w.ys + align_up((size_t)N * H * 4);
   w.part_gu = w.done + align_up((size_t)(w.n_zero_routed + w.n_zero_shared) * 4);
-  w.part_dn = w.part_gu + align_up(decode_part_bytes(w.tail_gu, w.nt, 2));
-  w.part_sgu = w.part_dn + align_up(decode_part_bytes(w.tail_dn, w.nt, 1));
+  w.part_dn = w.part_gu + align_up(w.tc ? tc_part_bytes(w.tail_gu, w.tn, 2) : decode_part_bytes(w.tail_gu, w.nt, 2));
+  w.part_sgu = w.part_dn + align_up(w.tc ? tc_part_bytes(w.tail_dn, w.tn, 1) : decode_part_bytes(w.tail_dn, w.nt, 1));
   w.part_sdn = w.part_sgu + align_up(decode_part_bytes(w.tail_sgu, w.nt_s, 2));
   w.total = w.part_sdn + align_up(decode_part_bytes(w.tail_sdn, w.nt_s, 1));
   return w;
@@ -124,10 +143,46 @@ int routed_decode(const cbmoe_experts* ex, const uint16_t* x, int N, const int32
                   float limit, uint8_t* ws, const DecodeWorkspace& W, cudaStream_t stream) {
   int32_t* plan = reinterpret_cast<int32_t*>(ws + W.plan);
   int* done = reinterpret_cast<int*>(ws + W.done);
-  int rc = launch_route_plan(idx, w, N, k, ex->E, 1, 8 * W.nt, plan, stream, done, W.n_zero_routed);
+  int rc = launch_route_plan(idx, w, N, k, ex->E, 1, W.tc ? W.tn : 8 * W.nt, plan, stream, done, W.n_zero_routed);
   if (rc) return rc;
   uint16_t* h = reinterpret_cast<uint16_t*>(ws + W.h);
   float* ys = reinterpret_cast<float*>(ws + W.y);
+  if (W.tc) {
+    uint16_t* xs = reinterpret_cast<uint16_t*>(ws + W.xs);
+    rc = launch_gather_perm(x, ex->H, plan + W.L.off[7], W.Rp, xs, stream);
+    if (rc) return rc;
+    TcParams t{};
+    t.wq = static_cast<const uint8_t*>(ex->gateup_idx);
+    t.cb = static_cast<const uint32_t*>(ex->gateup_cb);
+    t.rows = ex->I;
+    t.K = ex->H;
+    t.pass_expert = plan + W.L.off[10];
+    t.pass_row0 = plan + W.L.off[11];
+    t.pass_cnt = plan + W.L.off[12];
+    t.n_pass = plan + W.L.off[5];
+    t.E = ex->E;
+    t.limit = limit;
+    t.h_out = h;
+    t.h_plane = (size_t)W.Rp * ex->I;
+    t.sched = done;
+    t.done = done + 2;
+    t.part = reinterpret_cast<float*>(ws + W.part_gu);
+    t.tail_items = W.tail_gu;
+    rc = tc_cb3_gateup(t, xs, W.Rp, W.tn, stream);
+    if (rc) return rc;
+    TcParams d = t;
+    d.wq = static_cast<const uint8_t*>(ex->down_idx);
+    d.cb = static_cast<const uint32_t*>(ex->down_cb);
+    d.rows = ex->H;
+    d.K = ex->I;
+    d.h_out = nullptr;
+    d.y_out = ys;
+    d.sched = done + 1;
+    d.done = done + 2 + 4 * W.tail_gu;
+    d.part = reinterpret_cast<float*>(ws + W.part_dn);
+    d.tail_items = W.tail_dn;
+    return tc_cb3_down(d, h, h + t.h_plane, W.Rp, W.tn, stream);
+  }
 
   DecodeParams p = base_params();
   p.wq = static_cast<const uint8_t*>(ex->gateup_idx);
@@ -271,7 +326,8 @@ int pick_path(int N, int k, int path) {
 
 GroupedWorkspace grouped_workspace(int E, int H, int I, int N, int k) {
   GroupedWorkspace w;
-  w.L = host_plan_layout(N, k, E, 1, kGrpTileN);
+  w.tn = grp_pass_tokens((long long)N * k, E);
+  w.L = host_plan_layout(N, k, E, 1, w.tn);
   w.Rp = (int)(w.L.off[8] - w.L.off[7]);
   w.plan = 0;
   w.xs = align_up((size_t)w.L.off[13] * 4);
@@ -287,7 +343,7 @@ GroupedWorkspace grouped_workspace(int E, int H, int I, int N, int k) {
 int routed_grouped(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx, const float* w, int k,
                    float limit, uint8_t* ws, const GroupedWorkspace& W, cudaStream_t stream) {
   int32_t* plan = reinterpret_cast<int32_t*>(ws + W.plan);
-  int rc = launch_route_plan(idx, w, N, k, ex->E, 1, kGrpTileN, plan, stream);
+  int rc = launch_route_plan(idx, w, N, k, ex->E, 1, W.tn, plan, stream);
   if (rc) return rc;
   uint16_t* xs = reinterpret_cast<uint16_t*>(ws + W.xs);
   uint16_t* h = reinterpret_cast<uint16_t*>(ws + W.h);
@@ -306,7 +362,7 @@ int routed_grouped(const cbmoe_experts* ex, const uint16_t* x, int N, const int3
   p.E = ex->E;
   p.limit = limit;
   p.out = h;
-  rc = grouped_cb3_gateup(p, xs, W.Rp, stream);
+  rc = grouped_cb3_gateup(p, xs, W.Rp, W.tn, stream);
   if (rc) return rc;
   GroupedParams d = p;
   d.wq = static_cast<const uint8_t*>(ex->down_idx);
@@ -314,7 +370,7 @@ int routed_grouped(const cbmoe_experts* ex, const uint16_t* x, int N, const int3
   d.rows = ex->H;
   d.K = ex->I;
   d.out = ys;
-  return grouped_cb3_down(d, h, W.Rp, stream);
+  return grouped_cb3_down(d, h, W.Rp, W.tn, stream);
 }
 
 }  // namespace lyr
@@ -373,16 +429,19 @@ extern "C" int cbmoe_device_errors(int clear, int* out_host) {
 extern "C" size_t cbmoe_workspace_bytes(const cbmoe_experts* ex, int N, int k, int path) {
   if (!ex || N < 0 || k <= 0 || ex->E <= 0) return 0;
   if (pick_path(N, k, path) == CBMOE_PATH_GROUPED) return grouped_workspace(ex->E, ex->H, ex->I, N, k).total;
-  return decode_workspace(ex->E, ex->H, ex->I, N, k).total;
+  return decode_workspace(ex->E, ex->H, ex->I, N, k, -1, path == CBMOE_PATH_DECODE_TC).total;
 }
 
 static int check_common(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx, const float* w,
                         int k, int path) {
   if (!experts_ok(ex) || N < 0 || k <= 0 || k > 64) return CBMOE_ERR_INVALID;
   if (N > 0 && (!x || !idx || !w || !aligned16(x))) return CBMOE_ERR_INVALID;
-  if (path != CBMOE_PATH_AUTO && path != CBMOE_PATH_DECODE && path != CBMOE_PATH_GROUPED) return CBMOE_ERR_INVALID;
+  if (path != CBMOE_PATH_AUTO && path != CBMOE_PATH_DECODE && path != CBMOE_PATH_GROUPED &&
+      path != CBMOE_PATH_DECODE_TC)
+    return CBMOE_ERR_INVALID;
   if (pick_path(N, k, path) == CBMOE_PATH_GROUPED && (ex->I % kGrpTileM || ex->H % kGrpTileM || N > (1 << 24)))
     return CBMOE_ERR_UNSUPPORTED;
+  if (path == CBMOE_PATH_DECODE_TC && (ex->I % kTcTileM || ex->H % kTcTileM)) return CBMOE_ERR_UNSUPPORTED;
   return CBMOE_OK;
 }
 
@@ -403,7 +462,7 @@ extern "C" int cbmoe_experts_apply(const cbmoe_experts* ex, const uint16_t* x, i
     return launch_combine_bf16(reinterpret_cast<const uint16_t*>(ws + G.y), plan + G.L.off[9], w, N, k, ex->H,
                                nullptr, y, nullptr, stream);
   }
-  const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k);
+  const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k, -1, path == CBMOE_PATH_DECODE_TC);
   if (!workspace || workspace_bytes < W.total) return CBMOE_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   rc = routed_decode(ex, x, N, idx, w, k, limit, ws, W, stream);
@@ -454,7 +513,7 @@ extern "C" int cbmoe_moe_layer(const cbmoe_experts* ex, const cbmoe_shared* sh, 
     return launch_combine_bf16(reinterpret_cast<const uint16_t*>(ws + G.y), plan + G.L.off[9], w, N, k, ex->H, sy,
                                nullptr, out, stream);
   }
-  const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k);
+  const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k, -1, path == CBMOE_PATH_DECODE_TC);
   if (!workspace || workspace_bytes < W.total) return CBMOE_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   SideStream* side = nullptr;

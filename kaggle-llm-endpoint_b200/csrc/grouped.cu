@@ -3,7 +3,10 @@
 // (quant8.dequant_tree + dot, quant8.py:91-99).
 //
 //   D[w, t] = sum_k W_e[w, k] * X[t, k]     w: 128 weight rows of expert e (tcgen05 M = 128)
-//                                           t: up to 128 sorted token rows routed to e (tcgen05 N)
+//                                           t: up to TN sorted token rows routed to e (tcgen05 N): 256 for the
+//                                              routed CB3 passes, 128 / 256 for the int8 projections
+// A 128 x 16 slice of A costs the tensor core about as long whatever N (up to 256) it meets, so the widest pass
+// that the accumulators allow does the most work per dequantized tile.
 // The weights are dequantized ONCE per (pass, 128-row tile) straight into the tensor core's shared-memory
 // operand layout; the tokens come in by TMA. One CTA per SM, 11 warps:
 //   warp 0       packed-weight producer: bulk copies of CB3K / W8K bits (+ codebooks / scales) into a ring
@@ -12,8 +15,8 @@
 //   warps 3-6    dequant: packed bits -> bf16 A tiles (the decode kernels' register dequant) -> shared memory
 //   warps 7-10   epilogue: tcgen05.ld of the accumulators -> SwiGLU (gate/up) or store -> bf16 rows
 // Barriers: per MMA stage full (4 dequant warps + token TMA) / empty (MMA commit); per packed slot full / empty;
-// tmem_full[2] (MMA commit) / tmem_empty[2] (4 epilogue warps): two accumulator buffers, so the epilogue of one
-// item overlaps the MMAs of the next. Every wait is bounded; a role that gives up sets
+// tmem_full / tmem_empty (MMA commit / 4 epilogue warps) per accumulator buffer: two buffers where they fit TMEM,
+// so the epilogue of one item overlaps the MMAs of the next (gate/up with 256-token passes has one). Every wait is bounded; a role that gives up sets
 // CBMOE_DEVERR_TIMEOUT and falls through to the final barrier, after which warp 1 frees TMEM.
 // Items (pass, 128-row tile) are dealt round-robin to the persistent CTAs. No multicast anywhere.
 #include <cudaTypedefs.h>
@@ -46,9 +49,13 @@ struct GrpCfg {
   static constexpr int kBTile = TN * 128;                                // 16 / 32 KB
   static constexpr int kStage = NMAT * kATile + kBTile;
   static constexpr int kNStage = (FMT == kFmtW8) ? ((NMAT == 2 || TN == 256) ? 3 + (TN == 256) : 5)
-                                                 : ((NMAT == 2) ? 4 : 6);
+                                                 : (TN == 256 ? (NMAT == 2 ? 3 : 4) : (NMAT == 2 ? 4 : 6));
   static constexpr int kAccCols = NMAT * TN;                             // one accumulator buffer
-  static constexpr int kTmemCols = 2 * kAccCols;                         // double-buffered
+  // Two buffers (the epilogue of one item overlaps the MMAs of the next) where they fit the 512 TMEM columns;
+  // gate/up with 256-token passes has one, so its epilogue and the next item's MMAs take turns.
+  static constexpr int kAccBufs = 2 * kAccCols <= 512 ? 2 : 1;
+  static constexpr int kTmemCols = kAccBufs * kAccCols;
+  static_assert(kAccCols <= 512, "TMEM budget");
   static constexpr int kBarOff = kNStage * kStage + kNpk * kPkBytes;
   static constexpr int kSmem = 1024 + kBarOff + 256;                     // +1024: manual 1 KB alignment
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
@@ -203,9 +210,9 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grouped_kernel(const GroupedPa
         if (!item_ok(p, it)) continue;
         const int n = (it.cnt + 15) & ~15;
         const uint32_t idesc = idesc_bf16_m128(n);
-        const int buf = local & 1;
+        const int buf = (int)(local % C::kAccBufs);
         const uint32_t acc = tmem + buf * C::kAccCols;
-        if (!mbar_wait(&tm_empty[buf], ((local >> 1) & 1) ^ 1)) goto done;
+        if (!mbar_wait(&tm_empty[buf], ((local / C::kAccBufs) & 1) ^ 1)) goto done;
         tc_fence_after();
         for (int ks = 0; ks < KS64; ++ks) {
           if (!mbar_wait(&full[st], ph)) goto done;
@@ -344,8 +351,8 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grouped_kernel(const GroupedPa
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
       const ItemInfo it = grp_item<TN>(p, item);
       if (!item_ok(p, it)) continue;
-      const int buf = local & 1;
-      if (!mbar_wait(&tm_full[buf], (local >> 1) & 1)) goto done;
+      const int buf = (int)(local % C::kAccBufs);
+      if (!mbar_wait(&tm_full[buf], (local / C::kAccBufs) & 1)) goto done;
       tc_fence_after();
       const int wrow = it.rt * kGrpTileM + 32 * q + lane;
       const uint32_t tbase = tmem + buf * C::kAccCols + ((uint32_t)(32 * q) << 16);
@@ -518,11 +525,15 @@ int grid_of(long long total) {
 
 }  // namespace
 
-int grouped_cb3_gateup(const GroupedParams& p, const void* b, int b_rows, cudaStream_t s) {
-  return launch_grouped<kFmtCB3, 2, kGrpEpiSwiglu, kGrpTileN>(p, b, b_rows, kProfGrpCb3GateUp, s);
+int grouped_cb3_gateup(const GroupedParams& p, const void* b, int b_rows, int tn, cudaStream_t s) {
+  if (tn == 128) return launch_grouped<kFmtCB3, 2, kGrpEpiSwiglu, 128>(p, b, b_rows, kProfGrpCb3GateUp, s);
+  if (tn == 256) return launch_grouped<kFmtCB3, 2, kGrpEpiSwiglu, 256>(p, b, b_rows, kProfGrpCb3GateUp, s);
+  return CBMOE_ERR_INVALID;
 }
-int grouped_cb3_down(const GroupedParams& p, const void* b, int b_rows, cudaStream_t s) {
-  return launch_grouped<kFmtCB3, 1, kGrpEpiStore, kGrpTileN>(p, b, b_rows, kProfGrpCb3Down, s);
+int grouped_cb3_down(const GroupedParams& p, const void* b, int b_rows, int tn, cudaStream_t s) {
+  if (tn == 128) return launch_grouped<kFmtCB3, 1, kGrpEpiStore, 128>(p, b, b_rows, kProfGrpCb3Down, s);
+  if (tn == 256) return launch_grouped<kFmtCB3, 1, kGrpEpiStore, 256>(p, b, b_rows, kProfGrpCb3Down, s);
+  return CBMOE_ERR_INVALID;
 }
 int grouped_w8_gateup(const GroupedParams& p, const void* b, int b_rows, cudaStream_t s) {
   return launch_grouped<kFmtW8, 2, kGrpEpiSwiglu, 128>(p, b, b_rows, kProfGrpW8GateUp, s);

@@ -10,7 +10,11 @@ constexpr int kGrpEpiSwiglu = 0;   // NMAT = 2: out = bf16(swiglu_clamped(gate, 
 constexpr int kGrpEpiStore = 1;    // NMAT = 1: out = bf16(acc)
 constexpr int kGrpEpiStoreF32 = 2; // NMAT = 1: out_f32 = acc
 constexpr int kGrpTileM = 128;     // weight rows per tile (tcgen05 M)
-constexpr int kGrpTileN = 128;     // token rows per pass (tcgen05 N); two accumulator buffers fit TMEM
+// Token rows per routed CB3 pass (tcgen05 N). A 128 x 16 slice of weights costs the tensor core about as long for
+// N = 16 as for N = 256, so experts with many rows take 256-row passes; with few rows (a pass holds them all
+// either way) 128-row passes keep two accumulator buffers for gate/up, so the epilogue overlaps the next item.
+constexpr int kGrpTileN = 256;
+inline int grp_pass_tokens(long long S, int E) { return E > 0 && S > 128LL * E ? 256 : 128; }
 
 struct GroupedParams {
   const uint8_t* wq;       // CB3K index bits or W8K int8, unit layout (layout.cuh)
@@ -30,8 +34,9 @@ struct GroupedParams {
   float* out_f32;          // kGrpEpiStoreF32
 };
 
-int grouped_cb3_gateup(const GroupedParams& p, const void* b, int b_rows, cudaStream_t s);
-int grouped_cb3_down(const GroupedParams& p, const void* b, int b_rows, cudaStream_t s);
+// tn: token rows per pass of the routing plan (128 or 256).
+int grouped_cb3_gateup(const GroupedParams& p, const void* b, int b_rows, int tn, cudaStream_t s);
+int grouped_cb3_down(const GroupedParams& p, const void* b, int b_rows, int tn, cudaStream_t s);
 int grouped_w8_gateup(const GroupedParams& p, const void* b, int b_rows, cudaStream_t s);
 int grouped_w8_store(const GroupedParams& p, const void* b, int b_rows, cudaStream_t s);
 int grouped_w8_store_f32(const GroupedParams& p, const void* b, int b_rows, cudaStream_t s);

@@ -3,6 +3,7 @@
 #pragma once
 #include "decode.cuh"
 #include "grouped.cuh"
+#include "tcdecode.cuh"
 
 namespace cbmoe {
 namespace lyr {
@@ -13,7 +14,9 @@ struct PlanLayoutHost {
 
 // Workspace of the decode path (layout documented at decode_workspace in capi.cu).
 struct DecodeWorkspace {
-  size_t plan, h, y, hs, ys, done, part_gu, part_dn, part_sgu, part_sdn, total;
+  size_t plan, xs, h, y, hs, ys, done, part_gu, part_dn, part_sgu, part_sdn, total;
+  int tc;                                     // routed experts on the tcgen05 decode kernels (tcdecode.cu)
+  int tn;                                     // their token rows per pass
   int nt, nt_s, Rp, P, Ps, RB_gu, RB_dn;
   int tail_gu, tail_dn, tail_sgu, tail_sdn;   // partial-sum space of each launch, in tail items
   int n_zero_routed, n_zero_shared;           // arrival counters (words)
@@ -26,6 +29,7 @@ constexpr int kDecodeMaxCtasPerSm = 4;
 struct GroupedWorkspace {
   size_t plan, xs, h, y, hs, sy, total;
   int Rp;
+  int tn;                                     // token rows per routed pass (grp_pass_tokens)
   PlanLayoutHost L;
 };
 
@@ -56,7 +60,8 @@ PlanLayoutHost host_plan_layout(int T, int k, int E, int tm, int pass_tokens);
 int decode_nt(int N);
 int decode_nt_routed(int N, int k, int E);
 // slots_hint: the slots expected to be real when N*k counts empty ones too (< 0: N*k); picks the token tile.
-DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k, long long slots_hint = -1);
+// tc: routed experts on the tcgen05 decode kernels (CBMOE_PATH_DECODE_TC) instead of the mma.sync ones.
+DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k, long long slots_hint = -1, int tc = 0);
 GroupedWorkspace grouped_workspace(int E, int H, int I, int N, int k);
 int pick_path(int N, int k, int path);
 bool aligned16(const void* p);

@@ -142,31 +142,33 @@ def _pack(cbmoe, L):
                             shared_to_gpu(L["shared"]))
 
 
+@pytest.mark.parametrize("path", ["decode", "decode_tc"])
 @pytest.mark.parametrize("N,k,E,zipf", [(1, 8, 16, None), (3, 4, 16, None), (8, 8, 24, None), (20, 6, 16, 1.1),
                                         (64, 8, 32, 1.1), (40, 2, 4, None)])
-def test_experts_apply_decode(cbmoe, N, k, E, zipf):
+def test_experts_apply_decode(cbmoe, N, k, E, zipf, path):
     H, I = 512, 256
     rng, L = _layer(N * 31 + E, E, H, I)
     x = gen.activations(rng, N, H)
     idx, w = gen.routing(rng, N, E, k, zipf=zipf)
     p = _pack(cbmoe, L)
-    fetch = cbmoe.ResidentFetch(path="decode")
+    fetch = cbmoe.ResidentFetch(path=path)
     y = fetch.apply(p, t_bf16(x), torch.from_numpy(idx).cuda(), torch.from_numpy(w).cuda(), 0, gen.LIMIT)
     want = moe.decode_apply(x.astype(np.float32), idx, w, L["gate"], L["up"], L["down"], gen.LIMIT)
     assert moe.max_rel_err(y.cpu().numpy(), want) < LAYER_TOL
     _no_device_errors(cbmoe)
 
 
+@pytest.mark.parametrize("path", ["decode", "decode_tc"])
 @pytest.mark.parametrize("axis", [1, 0])
 @pytest.mark.parametrize("N", [1, 8, 24])
-def test_moe_layer_decode(cbmoe, N, axis):
+def test_moe_layer_decode(cbmoe, N, axis, path):
     E, H, I, k = 16, 512, 256, 8
     rng, L = _layer(N + 7 * axis, E, H, I, axis)
     x = gen.activations(rng, N, H)
     idx, w = gen.routing(rng, N, E, k)
     p = _pack(cbmoe, L)
     out = cbmoe.moe_dense(p, t_bf16(x), torch.from_numpy(idx).cuda(), torch.from_numpy(w).cuda(), gen.LIMIT,
-                          cbmoe.ResidentFetch(path="decode"))
+                          cbmoe.ResidentFetch(path=path))
     want = moe.moe_layer(x.astype(np.float32), idx, w, L["gate"], L["up"], L["down"], L["shared"], gen.LIMIT)
     assert out.dtype == torch.bfloat16
     assert moe.max_rel_err(out.float().cpu().numpy(), want) < LAYER_TOL

@@ -1,7 +1,8 @@
 """Parity at the benchmark's full layer size (needs a B200: -m gpu): E = 160 CB3 experts, hidden 5120,
 intermediate 1536, top-8, int8 shared expert, limit 10, through the library against the C oracle
 (oracle/cbmoe_cpu.c, fp32, checked against the NumPy oracle in test_oracle.py) on the same seeded inputs:
-config 1 (8 tokens, decode), config 2 (64 tokens with Zipf(1.1)-skewed routing, decode and grouped) and
+config 1 (8 tokens, decode), config 2 (64 tokens with Zipf(1.1)-skewed routing, decode and grouped), both also
+on the tcgen05 decode kernels (path decode_tc), and
 config 3 (4096 tokens on the grouped tensor-core path, checked on a sample of token rows; the layer is
 independent per token). Bar: max |got - want| / max |want| <= 1e-2 (bf16 out, fp32 accumulation)."""
 import numpy as np
@@ -41,16 +42,18 @@ def _run(cbmoe, p, x, idx, w, path):
     return out.float().cpu().numpy()
 
 
-def test_config1_decode_layer(setup):
-    cbmoe, L, p, rng = setup
+@pytest.mark.parametrize("path", ["decode", "decode_tc"])
+def test_config1_decode_layer(setup, path):
+    cbmoe, L, p, _ = setup
+    rng = np.random.default_rng(8)
     x = gen.activations(rng, 8, H)
     idx, w = gen.routing(rng, 8, E, K)
-    got = _run(cbmoe, p, x, idx, w, "decode")
+    got = _run(cbmoe, p, x, idx, w, path)
     assert moe.max_rel_err(got, _want(L, x, idx, w)) < TOL
     assert cbmoe.device_errors(clear=True) == 0
 
 
-@pytest.mark.parametrize("path", ["decode", "grouped"])
+@pytest.mark.parametrize("path", ["decode", "grouped", "decode_tc"])
 def test_config2_skewed_batch(setup, path):
     cbmoe, L, p, _ = setup
     rng = np.random.default_rng(64)
