@@ -194,6 +194,21 @@ int cbmoe_ep_layer(void* comm, int nranks, int rank, const cbmoe_experts* local,
 int cbmoe_ep_peer_init(void* comm, int nranks, int rank, int H, int capacity, cudaStream_t stream, void** peer_out);
 int cbmoe_ep_peer_destroy(void* peer);
 
+/* ---- llama.cpp IQ expert formats (the reference's real GLM-5.3-Flash tables) ----------------------------------
+ * Raw GGUF blocks of 256 weights, identified by their ggml_type numbers. Replaces iqquant.dequant_rows
+ * (engine/glm53/iqquant.py:230-235; the per-format dequant at :108-146): blocks [n_blocks][block bytes] ->
+ * out fp32 [n_blocks][256], bit for bit the reference's and gguf-py's values. `table` (device, fp32) is the
+ * format's lookup table as gguf-py defines it: IQ2_S grid [1024][8], IQ3_S grid [512][4], IQ4_XS the 16 IQ4_NL
+ * levels (cbmoe_iq_table_shape gives entries x width). out 16-byte aligned. Not yet a routed-expert path: the
+ * fused expert kernels take CB3 tables. */
+#define CBMOE_GGML_IQ3_S 21
+#define CBMOE_GGML_IQ2_S 22
+#define CBMOE_GGML_IQ4_XS 23
+size_t cbmoe_iq_block_bytes(int ggml_type);                        /* 82 / 110 / 136; 0 if not an IQ type here */
+int cbmoe_iq_table_shape(int ggml_type, int* entries, int* width);
+int cbmoe_iq_dequant(int ggml_type, const void* blocks, long long n_blocks, const float* table, float* out,
+                     cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
