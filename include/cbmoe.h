@@ -199,8 +199,7 @@ int cbmoe_ep_peer_destroy(void* peer);
  * (engine/glm53/iqquant.py:230-235; the per-format dequant at :108-146): blocks [n_blocks][block bytes] ->
  * out fp32 [n_blocks][256], bit for bit the reference's and gguf-py's values. `table` (device, fp32) is the
  * format's lookup table as gguf-py defines it: IQ2_S grid [1024][8], IQ3_S grid [512][4], IQ4_XS the 16 IQ4_NL
- * levels (cbmoe_iq_table_shape gives entries x width). out 16-byte aligned. Not yet a routed-expert path: the
- * fused expert kernels take CB3 tables. */
+ * levels (cbmoe_iq_table_shape gives entries x width). out 16-byte aligned. */
 #define CBMOE_GGML_IQ3_S 21
 #define CBMOE_GGML_IQ2_S 22
 #define CBMOE_GGML_IQ4_XS 23
@@ -208,6 +207,25 @@ size_t cbmoe_iq_block_bytes(int ggml_type);                        /* 82 / 110 /
 int cbmoe_iq_table_shape(int ggml_type, int* entries, int* width);
 int cbmoe_iq_dequant(int ggml_type, const void* blocks, long long n_blocks, const float* table, float* out,
                      cudaStream_t stream);
+
+/* Routed experts on raw GGUF IQ tables: ResidentFetch.apply with IQ qtypes (resident.py:100-120 over
+ * pallas_moe.moe_matvec, pallas_moe.py:238-307), per-matrix formats as in the reference's qtypes. Tables as in
+ * the GGUF: [E][rows][K/256][block bytes], gate/up rows = I over K = H, down rows = H over K = I (H, I multiples
+ * of 256); tables[] = each matrix's lookup table (see cbmoe_iq_dequant). Computes in fp32 like the reference:
+ * g, u = W x, h = swiglu_clamped(g, u, limit), y = sum_k w * (W_down h). y fp32 [N][H], 16-byte aligned. */
+typedef struct {
+  int E, H, I;
+  int gate_type, up_type, down_type;              /* CBMOE_GGML_IQ2_S / IQ3_S / IQ4_XS */
+  const void* gate;
+  const void* up;
+  const void* down;
+  const float* gate_table;
+  const float* up_table;
+  const float* down_table;
+} cbmoe_iq_experts;
+size_t cbmoe_iq_workspace_bytes(const cbmoe_iq_experts* ex, int N, int k);
+int cbmoe_iq_experts_apply(const cbmoe_iq_experts* ex, const uint16_t* x, int N, const int32_t* idx, const float* w,
+                           int k, float limit, float* y, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

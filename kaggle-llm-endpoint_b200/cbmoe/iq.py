@@ -1,14 +1,18 @@
-"""llama.cpp IQ expert formats on the GPU: the counterpart of the reference's iqquant.dequant_rows
-(engine/glm53/iqquant.py:230-235) over raw GGUF blocks (IQ2_S 82 B, IQ3_S 110 B, IQ4_XS 136 B per 256 weights),
-through cbmoe_iq_dequant. Bit for bit the reference's fp32 values. The lookup tables are gguf-py's grids (the
-reference loads the same ones, iq_grids_data.py), uploaded once per device.
+"""llama.cpp IQ expert formats on the GPU (the reference's real GLM-5.3-Flash tables; IQ2_S 82 B, IQ3_S 110 B,
+IQ4_XS 136 B per 256 weights):
+  * dequant_rows: the counterpart of iqquant.dequant_rows (engine/glm53/iqquant.py:230-235) through
+    cbmoe_iq_dequant, bit for bit the reference's fp32 values;
+  * pack_layer / apply: routed experts straight from the raw GGUF tables (ResidentFetch.apply with IQ qtypes,
+    resident.py:100-120), through cbmoe_iq_experts_apply, fp32 like the reference's kernel.
+The lookup tables are gguf-py's grids (the reference loads the same ones, iq_grids_data.py), uploaded once per
+device.
 """
 import ctypes
 
 import numpy as np
 import torch
 
-from ._lib import check, lib, ptr, require_cuda, stream_handle
+from ._lib import IqExperts, check, lib, ptr, require_cuda, stream_handle
 
 GGML_TYPE = {"IQ3_S": 21, "IQ2_S": 22, "IQ4_XS": 23}
 QK_K = 256
@@ -55,3 +59,49 @@ def dequant_rows(raw, qtype, ne0):
     check(lib().cbmoe_iq_dequant(GGML_TYPE[qtype], ptr(raw), n_blocks, ptr(table(qtype, raw.device)), ptr(out),
                                  stream_handle()), "cbmoe_iq_dequant")
     return out.view(-1, ne0)
+
+
+def pack_layer(gate, up, down, qtypes, E, H, I):
+    """Raw GGUF expert tables of one layer on the GPU (uint8, each [E][rows][K/256][block bytes] flattened: gate and
+    up I rows over H inputs, down H rows over I inputs) with their formats, qtypes = {"gate_q": "IQ2_S", "up_q":
+    ..., "down_q": ...} (the reference's per-layer qtypes) -> the table dict ResidentFetch.apply takes."""
+    require_cuda(gate, up, down)
+    assert H % QK_K == 0 and I % QK_K == 0, (H, I)
+    mats = {"gate_q": (gate, I, H), "up_q": (up, I, H), "down_q": (down, H, I)}
+    for key, (t, rows, K) in mats.items():
+        qt = qtypes[key]
+        assert qt in GGML_TYPE, qt
+        assert t.dtype == torch.uint8 and t.numel() == E * rows * (K // QK_K) * block_bytes(qt), \
+            (key, qt, t.numel(), E, rows, K)
+    return {"format": "IQ", "E": E, "H": H, "I": I, "qtypes": dict(qtypes),
+            "gate_q": gate.contiguous().view(-1), "up_q": up.contiguous().view(-1), "down_q": down.contiguous().view(-1),
+            "tables": {key: table(qtypes[key], gate.device) for key in mats}}
+
+
+def experts_struct(p):
+    q, t = p["qtypes"], p["tables"]
+    return IqExperts(p["E"], p["H"], p["I"], GGML_TYPE[q["gate_q"]], GGML_TYPE[q["up_q"]], GGML_TYPE[q["down_q"]],
+                     p["gate_q"].data_ptr(), p["up_q"].data_ptr(), p["down_q"].data_ptr(),
+                     t["gate_q"].data_ptr(), t["up_q"].data_ptr(), t["down_q"].data_ptr())
+
+
+_ws = {}
+
+
+def apply(p, x, idx, w, limit):
+    """x bf16 [N, H]; idx int32 [N, k]; w fp32 [N, k] -> fp32 [N, H] routed partial (resident.py:110-120)."""
+    N, k = idx.shape
+    ex = experts_struct(p)
+    y = torch.empty((N, p["H"]), dtype=torch.float32, device=x.device)
+    if N == 0:
+        return y
+    nbytes = lib().cbmoe_iq_workspace_bytes(ex, N, k)
+    key = (x.device, nbytes)
+    ws = _ws.get(key)
+    if ws is None:
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+        _ws.clear()
+        _ws[key] = ws
+    check(lib().cbmoe_iq_experts_apply(ex, ptr(x), N, ptr(idx), ptr(w), k, float(limit), ptr(y), ptr(ws),
+                                       ws.numel(), stream_handle()), "cbmoe_iq_experts_apply")
+    return y

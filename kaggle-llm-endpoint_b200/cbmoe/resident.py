@@ -13,7 +13,7 @@ asserts; there is no CPU fallback.
 """
 import torch
 
-from . import ops
+from . import iq, ops
 from ._lib import PATHS, Experts, Shared, check, lib, ptr, require_cuda, stream_handle
 
 CB3 = "CB3"
@@ -83,9 +83,10 @@ class ResidentFetch:
     def _check(self, p, x, idx, w, layer):
         require_cuda(x, idx, w)
         for key in ("gate_q", "up_q", "down_q"):
-            qt = self.qtypes.get(layer, {}).get(key, CB3)
-            if qt != CB3:
-                raise NotImplementedError(f"expert format {qt} is not built (CB3 only)")
+            have = p["qtypes"][key] if p.get("format") == "IQ" else CB3
+            qt = self.qtypes.get(layer, {}).get(key, have)
+            if qt != have:
+                raise ValueError(f"layer {layer} {key}: qtypes says {qt}, the tables hold {have}")
         N, k = idx.shape
         assert x.shape == (N, p["H"]), (x.shape, N, p["H"])
         assert w.shape == (N, k), (w.shape, (N, k))
@@ -98,6 +99,10 @@ class ResidentFetch:
     def apply(self, p, x, idx, w, layer, limit):
         """x [N, D]; idx [N, k] int32 into E; w [N, k] fp32 -> routed partial [N, D] in out_dtype."""
         N, k = self._check(p, x, idx, w, layer)
+        if p.get("format") == "IQ":   # raw GGUF IQ tables (cbmoe.iq.pack_layer)
+            y = iq.apply(p, x.to(torch.bfloat16).contiguous(), idx.to(torch.int32).contiguous(),
+                         w.to(torch.float32).contiguous(), limit)
+            return y if self.out_dtype == torch.float32 else y.to(self.out_dtype)
         xb = x.to(torch.bfloat16).contiguous()
         idx = idx.to(torch.int32).contiguous()
         w = w.to(torch.float32).contiguous()

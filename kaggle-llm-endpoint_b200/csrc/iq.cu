@@ -13,7 +13,7 @@
 // The lookup tables are the caller's (fp32, from gguf-py's grids): IQ2_S [1024][8], IQ3_S [512][4], IQ4_XS [16].
 #include <cuda_fp16.h>
 
-#include "layout.cuh"
+#include "layer.cuh"
 #include "profile.cuh"
 
 namespace cbmoe {
@@ -44,6 +44,43 @@ __device__ __forceinline__ float with_sign(float v, unsigned sign_byte, int k) {
   return ((sign_byte >> k) & 1u) ? -v : v;
 }
 
+// Weights 8*lane .. 8*lane+7 of one 256-weight block (see the file comment), fp32, products rounded once.
+template <int T>
+__device__ __forceinline__ void iq_lane8(const uint8_t* __restrict__ blk, int lane, const float* table,
+                                         float (&v)[8]) {
+  const float d = f16_at(blk);
+  if constexpr (T == CBMOE_GGML_IQ2_S) {
+    const int g = lane;
+    const int idx = blk[2 + g] | (((blk[66 + g / 4] >> (2 * (g % 4))) & 3) << 8);
+    const int s = (blk[74 + g / 4] >> (4 * ((g / 2) % 2))) & 15;
+    const unsigned sg = blk[34 + g];
+    const float db = __fmul_rn(__fmul_rn(d, 0.5f + (float)s), 0.25f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = with_sign(__fmul_rn(db, table[idx * 8 + k]), sg, k);
+  } else if constexpr (T == CBMOE_GGML_IQ3_S) {
+    const int m = lane / 4;   // 32-weight scale group
+    const int s = (blk[106 + m / 2] >> (4 * (m % 2))) & 15;
+    const float db = __fmul_rn(d, (float)(1 + 2 * s));
+    const unsigned sg = blk[74 + lane];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int G = 2 * lane + h;
+      const int idx = blk[2 + G] | (((blk[66 + G / 8] >> (G % 8)) & 1) << 8);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[4 * h + q] = with_sign(__fmul_rn(db, table[idx * 4 + q]), sg, 4 * h + q);
+    }
+  } else {
+    const int i = lane / 4, q = (lane % 4) * 8;   // sub-block, first position inside it
+    const int sh = blk[2] | (blk[3] << 8);
+    const int sc = (((blk[4 + i / 2] >> (4 * (i % 2))) & 15) | (((sh >> (2 * i)) & 3) << 4)) - 32;
+    const float dl = __fmul_rn(d, (float)sc);
+    const uint8_t* qs = blk + 8 + 16 * i + (q & 15);
+    const int shift = q >= 16 ? 4 : 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(dl, table[(qs[j] >> shift) & 15]);
+  }
+}
+
 template <int T>
 __global__ void iq_dequant_kernel(const uint8_t* __restrict__ blocks, long long n_blocks,
                                   const float* __restrict__ table, float* __restrict__ out) {
@@ -51,39 +88,8 @@ __global__ void iq_dequant_kernel(const uint8_t* __restrict__ blocks, long long 
   const int lane = threadIdx.x & 31;
   const long long warps = ((long long)gridDim.x * blockDim.x) >> 5;
   for (long long b = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; b < n_blocks; b += warps) {
-    const uint8_t* blk = blocks + b * BB;
-    const float d = f16_at(blk);
     float v[8];
-    if constexpr (T == CBMOE_GGML_IQ2_S) {
-      const int g = lane;
-      const int idx = blk[2 + g] | (((blk[66 + g / 4] >> (2 * (g % 4))) & 3) << 8);
-      const int s = (blk[74 + g / 4] >> (4 * ((g / 2) % 2))) & 15;
-      const unsigned sg = blk[34 + g];
-      const float db = __fmul_rn(__fmul_rn(d, 0.5f + (float)s), 0.25f);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = with_sign(__fmul_rn(db, table[idx * 8 + k]), sg, k);
-    } else if constexpr (T == CBMOE_GGML_IQ3_S) {
-      const int m = lane / 4;   // 32-weight scale group
-      const int s = (blk[106 + m / 2] >> (4 * (m % 2))) & 15;
-      const float db = __fmul_rn(d, (float)(1 + 2 * s));
-      const unsigned sg = blk[74 + lane];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int G = 2 * lane + h;
-        const int idx = blk[2 + G] | (((blk[66 + G / 8] >> (G % 8)) & 1) << 8);
-#pragma unroll
-        for (int p = 0; p < 4; ++p) v[4 * h + p] = with_sign(__fmul_rn(db, table[idx * 4 + p]), sg, 4 * h + p);
-      }
-    } else {
-      const int i = lane / 4, q = (lane % 4) * 8;   // sub-block, first position inside it
-      const int sh = blk[2] | (blk[3] << 8);
-      const int sc = (((blk[4 + i / 2] >> (4 * (i % 2))) & 15) | (((sh >> (2 * i)) & 3) << 4)) - 32;
-      const float dl = __fmul_rn(d, (float)sc);
-      const uint8_t* qs = blk + 8 + 16 * i + (q & 15);
-      const int shift = q >= 16 ? 4 : 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(dl, table[(qs[j] >> shift) & 15]);
-    }
+    iq_lane8<T>(blocks + b * BB, lane, table, v);
     float4* o = reinterpret_cast<float4*>(out + b * 256 + 8 * lane);
     o[0] = make_float4(v[0], v[1], v[2], v[3]);
     o[1] = make_float4(v[4], v[5], v[6], v[7]);
@@ -102,11 +108,208 @@ int launch_iq(const void* blocks, long long n_blocks, const float* table, float*
   return CBMOE_OK;
 }
 
+// ------------------------------------------------------------------------------------------ fused expert path
+// The decode composition of resident.py:110-120 (`_apply_kernel`: gate/up -> swiglu_clamped -> down -> weighted sum
+// of the slots) over raw GGUF IQ tables, computing in fp32 as the reference's moe_matvec does
+// (pallas_moe.py:238-307: on-the-fly dequant, fp32 products and sums). Rows of the routing plan are grouped in
+// passes of up to kIqPassTokens slots of one expert; an item is (pass, weight row), one warp per item: each lane
+// dequantizes its 8 weights of every 256-weight block of the row once (iq_lane8, the table in shared memory) and
+// multiply-adds them into one fp32 partial per token of the pass; a warp sum gives the row's outputs.
+//   gate, up: x = the slots' token rows (bf16, through the plan's row -> token map) -> g, u fp32 [sorted row][I]
+//   down:     x = swiglu_clamped(g, u) formed as it is read -> y fp32 [sorted row][H]; combine_kernel sums slots.
+constexpr int kIqPassTokens = 8;
+
+struct IqMatParams {
+  const uint8_t* w;          // raw blocks [E][rows][K / 256][block bytes]
+  const float* table;        // the format's lookup table (global; copied to shared memory per CTA)
+  int rows, K, E;
+  const int* pass_expert;
+  const int* pass_row0;
+  const int* pass_cnt;
+  const int* n_pass;
+  const uint16_t* x;         // gate/up: bf16 token rows [N][K]
+  const int* tok_row;        //   sorted row -> token
+  const float* g;            // down: fp32 gate and up outputs [sorted row][K]
+  const float* u;
+  float limit;
+  float* out;                // fp32 [sorted row][rows]
+};
+
+__device__ __forceinline__ void bf16x8(const uint4& q, float (&f)[8]) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+template <int T, int SWIGLU_IN>
+__global__ void __launch_bounds__(256) iq_matvec_kernel(const IqMatParams p) {
+  constexpr int BB = IqFmt<T>::kBytes;
+  constexpr int TAB = IqFmt<T>::kEntries * IqFmt<T>::kWidth;
+  __shared__ float tab[TAB];
+  for (int i = threadIdx.x; i < TAB; i += blockDim.x) tab[i] = p.table[i];
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int nblk = p.K / 256;
+  const long long items = (long long)(*p.n_pass) * p.rows;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long it = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += warps) {
+    const int pass = (int)(it / p.rows), r = (int)(it % p.rows);
+    const int e = p.pass_expert[pass], row0 = p.pass_row0[pass];
+    const int cnt = min(p.pass_cnt[pass], kIqPassTokens);
+    if (e < 0 || e >= p.E || cnt <= 0) continue;
+    const uint8_t* wrow = p.w + ((size_t)e * p.rows + r) * nblk * BB;
+    int tok[kIqPassTokens];
+#pragma unroll
+    for (int t = 0; t < kIqPassTokens; ++t) tok[t] = (!SWIGLU_IN && t < cnt) ? p.tok_row[row0 + t] : 0;
+    float acc[kIqPassTokens];
+#pragma unroll
+    for (int t = 0; t < kIqPassTokens; ++t) acc[t] = 0.f;
+    for (int b = 0; b < nblk; ++b) {
+      float v[8];
+      iq_lane8<T>(wrow + (size_t)b * BB, lane, tab, v);
+      const int k0 = b * 256 + 8 * lane;
+#pragma unroll
+      for (int t = 0; t < kIqPassTokens; ++t) {
+        if (t >= cnt) break;
+        float xv[8];
+        if constexpr (SWIGLU_IN) {
+          const size_t o = (size_t)(row0 + t) * p.K + k0;
+          const float4 g0 = *reinterpret_cast<const float4*>(p.g + o), g1 = *reinterpret_cast<const float4*>(p.g + o + 4);
+          const float4 u0 = *reinterpret_cast<const float4*>(p.u + o), u1 = *reinterpret_cast<const float4*>(p.u + o + 4);
+          const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+          const float uu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j) xv[j] = swiglu_clamped(gg[j], uu[j], p.limit);
+        } else {
+          bf16x8(*reinterpret_cast<const uint4*>(p.x + (size_t)tok[t] * p.K + k0), xv);
+        }
+        float a = acc[t];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a = fmaf(v[j], xv[j], a);
+        acc[t] = a;
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kIqPassTokens; ++t) {
+      if (t >= cnt) break;
+      float a = acc[t];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0) p.out[(size_t)(row0 + t) * p.rows + r] = a;
+    }
+  }
+}
+
+template <int SWIGLU_IN>
+int launch_iq_matvec(int type, const IqMatParams& p, long long max_items, int kind, cudaStream_t s) {
+  long long grid = (max_items + 7) / 8;
+  const long long cap = (long long)num_sms() * 8;
+  if (grid > cap) grid = cap;
+  if (grid < 1) grid = 1;
+  prof_begin(kind, s);
+  switch (type) {
+    case CBMOE_GGML_IQ2_S: iq_matvec_kernel<CBMOE_GGML_IQ2_S, SWIGLU_IN><<<(int)grid, 256, 0, s>>>(p); break;
+    case CBMOE_GGML_IQ3_S: iq_matvec_kernel<CBMOE_GGML_IQ3_S, SWIGLU_IN><<<(int)grid, 256, 0, s>>>(p); break;
+    default: iq_matvec_kernel<CBMOE_GGML_IQ4_XS, SWIGLU_IN><<<(int)grid, 256, 0, s>>>(p); break;
+  }
+  prof_end(kind, s);
+  CBMOE_CUDA_TRY(cudaGetLastError());
+  return CBMOE_OK;
+}
+
+struct IqWorkspace {
+  lyr::PlanLayoutHost L;
+  int Rp, P;
+  size_t plan, g, u, y, total;
+};
+
+IqWorkspace iq_workspace(const cbmoe_iq_experts* ex, int N, int k) {
+  IqWorkspace w;
+  w.L = lyr::host_plan_layout(N, k, ex->E, 1, kIqPassTokens);
+  w.Rp = (int)(w.L.off[8] - w.L.off[7]);
+  w.P = (int)(w.L.off[11] - w.L.off[10]);
+  w.plan = 0;
+  w.g = lyr::align_up((size_t)w.L.off[13] * 4);
+  w.u = w.g + lyr::align_up((size_t)w.Rp * ex->I * 4);
+  w.y = w.u + lyr::align_up((size_t)w.Rp * ex->I * 4);
+  w.total = w.y + lyr::align_up((size_t)w.Rp * ex->H * 4);
+  return w;
+}
+
+bool iq_experts_ok(const cbmoe_iq_experts* ex) {
+  auto ok_type = [](int t) { return cbmoe_iq_block_bytes(t) != 0; };
+  return ex && ex->E > 0 && ex->E <= 1024 && ex->H > 0 && ex->I > 0 && ex->H % 256 == 0 && ex->I % 256 == 0 &&
+         ok_type(ex->gate_type) && ok_type(ex->up_type) && ok_type(ex->down_type) && ex->gate && ex->up &&
+         ex->down && ex->gate_table && ex->up_table && ex->down_table;
+}
+
 }  // namespace
 
 }  // namespace cbmoe
 
 using namespace cbmoe;
+
+extern "C" size_t cbmoe_iq_workspace_bytes(const cbmoe_iq_experts* ex, int N, int k) {
+  if (!iq_experts_ok(ex) || N < 0 || k <= 0 || k > 64) return 0;
+  return iq_workspace(ex, N, k).total;
+}
+
+extern "C" int cbmoe_iq_experts_apply(const cbmoe_iq_experts* ex, const uint16_t* x, int N, const int32_t* idx,
+                                      const float* w, int k, float limit, float* y, void* workspace,
+                                      size_t workspace_bytes, cudaStream_t stream) {
+  if (!iq_experts_ok(ex) || N < 0 || k <= 0 || k > 64) return CBMOE_ERR_INVALID;
+  if (N == 0) return CBMOE_OK;
+  if (!x || !idx || !w || !y || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
+    return CBMOE_ERR_INVALID;
+  const IqWorkspace W = iq_workspace(ex, N, k);
+  if (!workspace || workspace_bytes < W.total) return CBMOE_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return CBMOE_ERR_INVALID;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* plan = reinterpret_cast<int32_t*>(ws + W.plan);
+  int rc = launch_route_plan(idx, w, N, k, ex->E, 1, kIqPassTokens, plan, stream);
+  if (rc) return rc;
+  float* g = reinterpret_cast<float*>(ws + W.g);
+  float* u = reinterpret_cast<float*>(ws + W.u);
+  float* ys = reinterpret_cast<float*>(ws + W.y);
+  IqMatParams p{};
+  p.rows = ex->I;
+  p.K = ex->H;
+  p.E = ex->E;
+  p.pass_expert = plan + W.L.off[10];
+  p.pass_row0 = plan + W.L.off[11];
+  p.pass_cnt = plan + W.L.off[12];
+  p.n_pass = plan + W.L.off[5];
+  p.x = x;
+  p.tok_row = plan + W.L.off[7];
+  p.limit = limit;
+  const long long items_gu = (long long)W.P * ex->I, items_dn = (long long)W.P * ex->H;
+  p.w = static_cast<const uint8_t*>(ex->gate);
+  p.table = ex->gate_table;
+  p.out = g;
+  rc = launch_iq_matvec<0>(ex->gate_type, p, items_gu, kProfOther, stream);
+  if (rc) return rc;
+  p.w = static_cast<const uint8_t*>(ex->up);
+  p.table = ex->up_table;
+  p.out = u;
+  rc = launch_iq_matvec<0>(ex->up_type, p, items_gu, kProfOther, stream);
+  if (rc) return rc;
+  IqMatParams d = p;
+  d.w = static_cast<const uint8_t*>(ex->down);
+  d.table = ex->down_table;
+  d.rows = ex->H;
+  d.K = ex->I;
+  d.x = nullptr;
+  d.tok_row = nullptr;
+  d.g = g;
+  d.u = u;
+  d.out = ys;
+  rc = launch_iq_matvec<1>(ex->down_type, d, items_dn, kProfOther, stream);
+  if (rc) return rc;
+  return launch_combine(ys, plan + W.L.off[9], w, N, k, ex->H, nullptr, y, nullptr, stream);
+}
 
 extern "C" size_t cbmoe_iq_block_bytes(int ggml_type) {
   switch (ggml_type) {

@@ -105,3 +105,22 @@ def random_blocks(rng, n, qtype, dmin=1e-3, dmax=2e-2):
     b = rng.integers(0, 256, (n, bb), dtype=np.uint8)
     b[:, 0:2] = np.frombuffer(rng.uniform(dmin, dmax, n).astype(np.float16).tobytes(), np.uint8).reshape(n, 2)
     return b
+
+
+def experts_dense(raw, qtype, E, rows, K, tabs=None):
+    """Raw GGUF expert table ([E][rows][K/256][block bytes] bytes) -> fp32 [E, rows, K]."""
+    return dequant_rows(raw, qtype, K, tabs).reshape(E, rows, K)
+
+
+def decode_apply(x, idx, w, Wg, Wu, Wd, limit):
+    """resident.py:110-120 over dense fp32 experts (Wg, Wu [E, I, H], Wd [E, H, I]), in float64: per (token, slot)
+    g = Wg x, u = Wu x, h = swiglu_clamped(g, u), y += w * (Wd h). -> [N, H]."""
+    from oracle import moe
+    x = np.asarray(x, np.float64)
+    out = np.zeros((x.shape[0], Wd.shape[1]), np.float64)
+    for n in range(x.shape[0]):
+        for j in range(idx.shape[1]):
+            e = int(idx[n, j])
+            h = moe.swiglu_clamped(Wg[e].astype(np.float64) @ x[n], Wu[e].astype(np.float64) @ x[n], limit)
+            out[n] += float(w[n, j]) * (Wd[e].astype(np.float64) @ h)
+    return out
