@@ -58,9 +58,10 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="resident layers cycled by the steps (profiling "
                     "captures use 1 to keep device memory small)")
-    ap.add_argument("--workload", choices=["decode", "prefill", "ep"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "ep", "iq"], default="decode",
                     help="decode = config 1 (the default bench line); prefill = config 3 (4096 tokens, tcgen05 path); "
-                         "ep = config 4 (4 layers, 256 tokens, experts sharded over the GPUs, strong scaling)")
+                         "ep = config 4 (4 layers, 256 tokens, experts sharded over the GPUs, strong scaling); "
+                         "iq = the config-1 batch on the reference's GGUF IQ table formats (routed experts, 1 GPU)")
     ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
                     help="N > 1: dispatch/return through peer memory over NVLink, or NCCL send/recv")
     ap.add_argument("--ep-path", choices=["auto", "decode", "grouped"], default="auto",
@@ -819,8 +820,89 @@ def run_ep_stack(args):
         dist.destroy_process_group()
 
 
+def run_iq(args):
+    """The config-1 batch (8 tokens, top-8, E=160, H=5120, I=1536) on the reference's real table formats: raw GGUF
+    IQ2_S gate/up and IQ3_S down (the mix of its blk.3 sample), routed experts through ResidentFetch.apply
+    (cbmoe_iq_experts_apply, fp32). One GPU; synthetic random blocks with f16 block scales in [1e-3, 2e-2]."""
+    import torch
+    import cbmoe
+    from cbmoe._lib import launch_count, profile_enable, profile_read
+
+    assert int(os.environ.get("WORLD_SIZE", "1")) == 1, "--workload iq runs on one GPU"
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    qtypes = {"gate_q": "IQ2_S", "up_q": "IQ2_S", "down_q": "IQ3_S"}
+    shapes = {"gate_q": (I, H), "up_q": (I, H), "down_q": (H, I)}
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+
+    def table(qt, rows, K):
+        bb = cbmoe.iq.block_bytes(qt)
+        n = E * rows * (K // 256)
+        t = torch.randint(0, 256, (n, bb), dtype=torch.uint8, device=dev, generator=g)
+        d = torch.empty(n, dtype=torch.float16, device=dev).uniform_(1e-3, 2e-2, generator=g)
+        t[:, 0:2] = d.view(torch.uint8).view(n, 2)
+        return t.view(-1)
+
+    n_layers = max(1, min(args.layers, 8))
+    layers = [cbmoe.iq.pack_layer(*(table(qtypes[k], *shapes[k]) for k in ("gate_q", "up_q", "down_q")), qtypes,
+                                  E, H, I) for _ in range(n_layers)]
+    per_expert = sum(shapes[k][0] * (shapes[k][1] // 256) * cbmoe.iq.block_bytes(qtypes[k]) for k in shapes)
+    batches = make_batches(torch, dev, 7, N_BATCHES)
+    distinct = [len(set(b[1].cpu().reshape(-1).tolist())) for b in batches]
+    fetch = cbmoe.ResidentFetch(qtypes={0: qtypes})
+    torch.cuda.synchronize()
+
+    def step(s):
+        x, idx, w = batches[s % N_BATCHES]
+        fetch.apply(layers[s % n_layers], x, idx, w, 0, LIMIT)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = launch_count()
+    with ClockSampler(0) as clocks:
+        ev0.record()
+        for s in range(args.steps):
+            step(args.warmup + s)
+        ev1.record()
+        torch.cuda.synchronize()
+    launches = launch_count() - l0
+    ms_step = ev0.elapsed_time(ev1) / args.steps
+    profile_enable(True)
+    profile_read(reset=True)
+    for s in range(args.steps):
+        step(args.warmup + s)
+    torch.cuda.synchronize()
+    prof = profile_read(reset=True)
+    profile_enable(False)
+    u_mean = sum(distinct[(args.warmup + s) % N_BATCHES] for s in range(args.steps)) / args.steps
+    algo = u_mean * per_expert + N_TOK * H * (2 + 4)
+    peak, peak_src = load_peaks()
+    achieved = algo / (ms_step / 1000.0) / 1e9
+    line = {"metric": "IQ routed experts tok/s (GGUF IQ2_S gate/up + IQ3_S down, config-1 batch)",
+            "value": N_TOK * 1000.0 / ms_step, "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config-1 batch on the reference's IQ table formats: 8 tokens, top-8, E=160, "
+                                   "H=5120, I=1536, routed experts only (no shared expert)",
+                       "qtypes": qtypes, "table_bytes_per_expert": per_expert,
+                       "l2": f"{n_layers} resident layers ({n_layers * E * per_expert / 1e9:.1f} GB) cycled"},
+            "clocks": clocks.summary(), "gpu_launches": launches,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": f"{peak_src} hbm_gbs (copy bandwidth)",
+                         "traffic": None,
+                         "algorithmic_bytes_per_step": algo, "distinct_experts_per_step": u_mean},
+            "kernels": {k: {"launches": n, "avg_us": 1000.0 * t / max(n, 1)} for k, (n, t) in prof.items()}}
+    print(json.dumps(line))
+
+
 def main():
     args = parse()
+    if args.workload == "iq" and args.impl == "ours":
+        run_iq(args)
+        return
     if args.workload == "prefill" and args.impl == "ours":
         run_prefill(args)
         return
