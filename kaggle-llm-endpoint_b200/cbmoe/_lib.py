@@ -134,7 +134,8 @@ def device_errors(clear=True):
 
 
 PROFILE_KINDS = ("plan", "cb3_gateup", "cb3_down", "cb3_single", "w8_gateup", "w8_down", "w8_single",
-                 "combine", "other", "grp_cb3_gateup", "grp_cb3_down", "grp_w8_gateup", "grp_w8_store", "exchange")
+                 "combine", "other", "grp_cb3_gateup", "grp_cb3_down", "grp_w8_gateup", "grp_w8_store", "exchange",
+                 "iq_gateup", "iq_down")
 
 
 def profile_enable(on=True):

@@ -116,7 +116,8 @@ int launch_iq(const void* blocks, long long n_blocks, const float* table, float*
 // dequantizes its 8 weights of every 256-weight block of the row once (iq_lane8, the table in shared memory) and
 // multiply-adds them into one fp32 partial per token of the pass; a warp sum gives the row's outputs.
 //   gate, up: x = the slots' token rows (bf16, through the plan's row -> token map) -> g, u fp32 [sorted row][I]
-//   down:     x = swiglu_clamped(g, u) formed as it is read -> y fp32 [sorted row][H]; combine_kernel sums slots.
+//   h = swiglu_clamped(g, u) (elementwise, into g's buffer)
+//   down:     x = h (fp32 sorted rows) -> y fp32 [sorted row][H]; combine_kernel sums the slots.
 constexpr int kIqPassTokens = 8;
 
 struct IqMatParams {
@@ -129,9 +130,7 @@ struct IqMatParams {
   const int* n_pass;
   const uint16_t* x;         // gate/up: bf16 token rows [N][K]
   const int* tok_row;        //   sorted row -> token
-  const float* g;            // down: fp32 gate and up outputs [sorted row][K]
-  const float* u;
-  float limit;
+  const float* h;            // down: fp32 SwiGLU rows [sorted row][K]
   float* out;                // fp32 [sorted row][rows]
 };
 
@@ -144,7 +143,7 @@ __device__ __forceinline__ void bf16x8(const uint4& q, float (&f)[8]) {
   }
 }
 
-template <int T, int SWIGLU_IN>
+template <int T, int H_IN>
 __global__ void __launch_bounds__(256) iq_matvec_kernel(const IqMatParams p) {
   constexpr int BB = IqFmt<T>::kBytes;
   constexpr int TAB = IqFmt<T>::kEntries * IqFmt<T>::kWidth;
@@ -163,7 +162,7 @@ __global__ void __launch_bounds__(256) iq_matvec_kernel(const IqMatParams p) {
     const uint8_t* wrow = p.w + ((size_t)e * p.rows + r) * nblk * BB;
     int tok[kIqPassTokens];
 #pragma unroll
-    for (int t = 0; t < kIqPassTokens; ++t) tok[t] = (!SWIGLU_IN && t < cnt) ? p.tok_row[row0 + t] : 0;
+    for (int t = 0; t < kIqPassTokens; ++t) tok[t] = (!H_IN && t < cnt) ? p.tok_row[row0 + t] : 0;
     float acc[kIqPassTokens];
 #pragma unroll
     for (int t = 0; t < kIqPassTokens; ++t) acc[t] = 0.f;
@@ -175,14 +174,11 @@ __global__ void __launch_bounds__(256) iq_matvec_kernel(const IqMatParams p) {
       for (int t = 0; t < kIqPassTokens; ++t) {
         if (t >= cnt) break;
         float xv[8];
-        if constexpr (SWIGLU_IN) {
-          const size_t o = (size_t)(row0 + t) * p.K + k0;
-          const float4 g0 = *reinterpret_cast<const float4*>(p.g + o), g1 = *reinterpret_cast<const float4*>(p.g + o + 4);
-          const float4 u0 = *reinterpret_cast<const float4*>(p.u + o), u1 = *reinterpret_cast<const float4*>(p.u + o + 4);
-          const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-          const float uu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-#pragma unroll
-          for (int j = 0; j < 8; ++j) xv[j] = swiglu_clamped(gg[j], uu[j], p.limit);
+        if constexpr (H_IN) {
+          const float* hp = p.h + (size_t)(row0 + t) * p.K + k0;
+          const float4 h0 = *reinterpret_cast<const float4*>(hp), h1 = *reinterpret_cast<const float4*>(hp + 4);
+          xv[0] = h0.x; xv[1] = h0.y; xv[2] = h0.z; xv[3] = h0.w;
+          xv[4] = h1.x; xv[5] = h1.y; xv[6] = h1.z; xv[7] = h1.w;
         } else {
           bf16x8(*reinterpret_cast<const uint4*>(p.x + (size_t)tok[t] * p.K + k0), xv);
         }
@@ -203,7 +199,13 @@ __global__ void __launch_bounds__(256) iq_matvec_kernel(const IqMatParams p) {
   }
 }
 
-template <int SWIGLU_IN>
+// g[i] = swiglu_clamped(g[i], u[i], limit) over n elements (fp32, in place).
+__global__ void iq_swiglu_kernel(float* __restrict__ g, const float* __restrict__ u, long long n, float limit) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    g[i] = swiglu_clamped(g[i], u[i], limit);
+}
+
+template <int H_IN>
 int launch_iq_matvec(int type, const IqMatParams& p, long long max_items, int kind, cudaStream_t s) {
   long long grid = (max_items + 7) / 8;
   const long long cap = (long long)num_sms() * 8;
@@ -211,9 +213,9 @@ int launch_iq_matvec(int type, const IqMatParams& p, long long max_items, int ki
   if (grid < 1) grid = 1;
   prof_begin(kind, s);
   switch (type) {
-    case CBMOE_GGML_IQ2_S: iq_matvec_kernel<CBMOE_GGML_IQ2_S, SWIGLU_IN><<<(int)grid, 256, 0, s>>>(p); break;
-    case CBMOE_GGML_IQ3_S: iq_matvec_kernel<CBMOE_GGML_IQ3_S, SWIGLU_IN><<<(int)grid, 256, 0, s>>>(p); break;
-    default: iq_matvec_kernel<CBMOE_GGML_IQ4_XS, SWIGLU_IN><<<(int)grid, 256, 0, s>>>(p); break;
+    case CBMOE_GGML_IQ2_S: iq_matvec_kernel<CBMOE_GGML_IQ2_S, H_IN><<<(int)grid, 256, 0, s>>>(p); break;
+    case CBMOE_GGML_IQ3_S: iq_matvec_kernel<CBMOE_GGML_IQ3_S, H_IN><<<(int)grid, 256, 0, s>>>(p); break;
+    default: iq_matvec_kernel<CBMOE_GGML_IQ4_XS, H_IN><<<(int)grid, 256, 0, s>>>(p); break;
   }
   prof_end(kind, s);
   CBMOE_CUDA_TRY(cudaGetLastError());
@@ -284,18 +286,26 @@ extern "C" int cbmoe_iq_experts_apply(const cbmoe_iq_experts* ex, const uint16_t
   p.n_pass = plan + W.L.off[5];
   p.x = x;
   p.tok_row = plan + W.L.off[7];
-  p.limit = limit;
   const long long items_gu = (long long)W.P * ex->I, items_dn = (long long)W.P * ex->H;
   p.w = static_cast<const uint8_t*>(ex->gate);
   p.table = ex->gate_table;
   p.out = g;
-  rc = launch_iq_matvec<0>(ex->gate_type, p, items_gu, kProfOther, stream);
+  rc = launch_iq_matvec<0>(ex->gate_type, p, items_gu, kProfIqGateUp, stream);
   if (rc) return rc;
   p.w = static_cast<const uint8_t*>(ex->up);
   p.table = ex->up_table;
   p.out = u;
-  rc = launch_iq_matvec<0>(ex->up_type, p, items_gu, kProfOther, stream);
+  rc = launch_iq_matvec<0>(ex->up_type, p, items_gu, kProfIqGateUp, stream);
   if (rc) return rc;
+  {
+    const long long n = (long long)W.Rp * ex->I;
+    long long blocks = (n + 255) / 256;
+    if (blocks > (long long)num_sms() * 8) blocks = (long long)num_sms() * 8;
+    prof_begin(kProfIqGateUp, stream);
+    iq_swiglu_kernel<<<(int)blocks, 256, 0, stream>>>(g, u, n, limit);
+    prof_end(kProfIqGateUp, stream);
+    CBMOE_CUDA_TRY(cudaGetLastError());
+  }
   IqMatParams d = p;
   d.w = static_cast<const uint8_t*>(ex->down);
   d.table = ex->down_table;
@@ -303,10 +313,9 @@ extern "C" int cbmoe_iq_experts_apply(const cbmoe_iq_experts* ex, const uint16_t
   d.K = ex->I;
   d.x = nullptr;
   d.tok_row = nullptr;
-  d.g = g;
-  d.u = u;
+  d.h = g;
   d.out = ys;
-  rc = launch_iq_matvec<1>(ex->down_type, d, items_dn, kProfOther, stream);
+  rc = launch_iq_matvec<1>(ex->down_type, d, items_dn, kProfIqDown, stream);
   if (rc) return rc;
   return launch_combine(ys, plan + W.L.off[9], w, N, k, ex->H, nullptr, y, nullptr, stream);
 }

@@ -21,6 +21,8 @@ enum ProfKind {
   kProfGrpW8GateUp = 11,  // grouped_kernel<W8, gate+up, SWIGLU>
   kProfGrpW8Store = 12,   // grouped_kernel<W8, one matrix, STORE>
   kProfExchange = 13,     // expert-parallel NCCL dispatch or return (one send/recv group)
+  kProfIqGateUp = 14,     // iq_matvec_kernel over gate or up (raw GGUF IQ tables), and the SwiGLU between
+  kProfIqDown = 15,       // iq_matvec_kernel over down
   kProfKinds = 16
 };
 
