@@ -194,6 +194,13 @@ int cbmoe_ep_layer(void* comm, int nranks, int rank, const cbmoe_experts* local,
 int cbmoe_ep_peer_init(void* comm, int nranks, int rank, int H, int capacity, cudaStream_t stream, void** peer_out);
 int cbmoe_ep_peer_destroy(void* peer);
 
+/* MoE router, fused (replaces moe_route, engine/glm53/model.py:798-808, n_group == 1): x bf16 [N][D], router_w bf16
+ * [D][E] (x @ router_w), bias fp32 [E] -> idx int32 [N][k], w fp32 [N][k]: logits in fp32, s = sigmoid(logits),
+ * idx = top k of s + bias (largest first; the lower expert index first among equal choices), w = s[idx],
+ * normalized to sum 1 when norm_topk (w / (sum + 1e-20)), times scaling. E <= 256, k <= 32, k <= E. */
+int cbmoe_route(const uint16_t* x, int N, int D, const uint16_t* router_w, const float* bias, int E, int k,
+                int norm_topk, float scaling, int32_t* idx, float* w, cudaStream_t stream);
+
 /* ---- llama.cpp IQ expert formats (the reference's real GLM-5.3-Flash tables) ----------------------------------
  * Raw GGUF blocks of 256 weights, identified by their ggml_type numbers. Replaces iqquant.dequant_rows
  * (engine/glm53/iqquant.py:230-235; the per-format dequant at :108-146): blocks [n_blocks][block bytes] ->

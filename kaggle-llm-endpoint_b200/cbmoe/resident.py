@@ -134,3 +134,21 @@ class ResidentFetch:
 def moe_dense(p, x, idx, w, limit, fetch):
     """model.py:840-856 after `moe_route`: y = fetch.apply(...) + mlp_partial(shared), bf16 out (no TP reduce)."""
     return fetch.layer(p, x, idx, w, limit)
+
+
+def moe_route(x, router_w, bias, k, norm_topk=True, scaling=1.0):
+    """model.py:798-808 on the GPU (cbmoe_route): x [N, D] (bf16), router_w [D, E] (bf16), bias [E] ->
+    (idx int32 [N, k], w fp32 [N, k]); sigmoid scores, top k of scores + bias, weights = the chosen scores,
+    normalized when norm_topk, times scaling."""
+    require_cuda(x, router_w, bias)
+    N, D = x.shape
+    assert router_w.shape[0] == D and bias.shape == (router_w.shape[1],), (x.shape, router_w.shape, bias.shape)
+    E = router_w.shape[1]
+    xb = x.to(torch.bfloat16).contiguous()
+    wb = router_w.to(torch.bfloat16).contiguous()
+    bf = bias.to(torch.float32).contiguous()
+    idx = torch.empty((N, k), dtype=torch.int32, device=x.device)
+    w = torch.empty((N, k), dtype=torch.float32, device=x.device)
+    check(lib().cbmoe_route(ptr(xb), N, D, ptr(wb), ptr(bf), E, k, 1 if norm_topk else 0, float(scaling), ptr(idx),
+                            ptr(w), stream_handle()), "cbmoe_route")
+    return idx, w
