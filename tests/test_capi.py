@@ -65,3 +65,26 @@ def test_plan_layout_sizes(L):
     G = -(-S // tm) + E
     assert off[7] - off[6] >= G and off[8] - off[7] >= G * tm and off[10] - off[9] >= S
     assert L.cbmoe_plan_layout(8, 8, 2048, 1, 8, off) == -1      # more experts than the plan kernel supports
+
+
+def test_iq_and_route_host_side(L):
+    """The IQ-format and router entry points answer shape queries and reject bad calls without a GPU."""
+    from cbmoe._lib import IqExperts
+    assert (L.cbmoe_iq_block_bytes(22), L.cbmoe_iq_block_bytes(21), L.cbmoe_iq_block_bytes(23)) == (82, 110, 136)
+    assert L.cbmoe_iq_block_bytes(12) == 0                                    # Q4_K: not an IQ type here
+    e, w = ctypes.c_int(), ctypes.c_int()
+    for t, shape in ((22, (1024, 8)), (21, (512, 4)), (23, (16, 1))):
+        assert L.cbmoe_iq_table_shape(t, ctypes.byref(e), ctypes.byref(w)) == 0 and (e.value, w.value) == shape
+    assert L.cbmoe_iq_table_shape(12, ctypes.byref(e), ctypes.byref(w)) == -4   # unsupported
+    assert L.cbmoe_iq_dequant(12, None, 1, None, None, None) == -4
+    assert L.cbmoe_iq_dequant(22, None, -1, None, None, None) == -1
+    assert L.cbmoe_iq_dequant(22, None, 0, None, None, None) == 0             # nothing to do
+    ex = IqExperts(160, 5120, 1536, 22, 22, 21, 16, 16, 16, 16, 16, 16)
+    assert L.cbmoe_iq_workspace_bytes(ctypes.byref(ex), 8, 8) > 0
+    bad = IqExperts(160, 5000, 1536, 22, 22, 21, 16, 16, 16, 16, 16, 16)      # H not a multiple of 256
+    assert L.cbmoe_iq_workspace_bytes(ctypes.byref(bad), 8, 8) == 0
+    assert L.cbmoe_iq_experts_apply(ctypes.byref(bad), 16, 8, 16, 16, 8, 10.0, 16, None, 0, None) == -1
+    assert L.cbmoe_iq_experts_apply(ctypes.byref(ex), 16, 8, 16, 16, 8, 10.0, 16, None, 0, None) == -3   # workspace
+    assert L.cbmoe_route(None, 1, 64, None, None, 300, 8, 1, 1.0, None, None, None) == -1   # E > 256
+    assert L.cbmoe_route(None, 1, 64, None, None, 16, 17, 1, 1.0, None, None, None) == -1   # k > E
+    assert L.cbmoe_route(None, 0, 64, None, None, 16, 8, 1, 1.0, None, None, None) == 0     # nothing to do
