@@ -206,11 +206,14 @@ int cbmoe_route(const uint16_t* x, int N, int D, const uint16_t* router_w, const
  * (engine/glm53/iqquant.py:230-235; the per-format dequant at :108-146): blocks [n_blocks][block bytes] ->
  * out fp32 [n_blocks][256], bit for bit the reference's and gguf-py's values. `table` (device, fp32) is the
  * format's lookup table as gguf-py defines it: IQ2_S grid [1024][8], IQ3_S grid [512][4], IQ4_XS the 16 IQ4_NL
- * levels (cbmoe_iq_table_shape gives entries x width). out 16-byte aligned. */
+ * levels (cbmoe_iq_table_shape gives entries x width); Q2_K and Q3_K have none (0 x 0, table may be NULL).
+ * out 16-byte aligned. */
+#define CBMOE_GGML_Q2_K 10                                      /* the reference's MTP-layer experts */
+#define CBMOE_GGML_Q3_K 11
 #define CBMOE_GGML_IQ3_S 21
 #define CBMOE_GGML_IQ2_S 22
 #define CBMOE_GGML_IQ4_XS 23
-size_t cbmoe_iq_block_bytes(int ggml_type);                        /* 82 / 110 / 136; 0 if not an IQ type here */
+size_t cbmoe_iq_block_bytes(int ggml_type);          /* 84 / 110 / 110 / 82 / 136; 0 if not one of the five here */
 int cbmoe_iq_table_shape(int ggml_type, int* entries, int* width);
 int cbmoe_iq_dequant(int ggml_type, const void* blocks, long long n_blocks, const float* table, float* out,
                      cudaStream_t stream);
@@ -222,7 +225,7 @@ int cbmoe_iq_dequant(int ggml_type, const void* blocks, long long n_blocks, cons
  * g, u = W x, h = swiglu_clamped(g, u, limit), y = sum_k w * (W_down h). y fp32 [N][H], 16-byte aligned. */
 typedef struct {
   int E, H, I;
-  int gate_type, up_type, down_type;              /* CBMOE_GGML_IQ2_S / IQ3_S / IQ4_XS */
+  int gate_type, up_type, down_type;              /* CBMOE_GGML_IQ2_S / IQ3_S / IQ4_XS / Q2_K / Q3_K */
   const void* gate;
   const void* up;
   const void* down;

@@ -1,5 +1,5 @@
-"""llama.cpp IQ expert formats on the GPU (the reference's real GLM-5.3-Flash tables; IQ2_S 82 B, IQ3_S 110 B,
-IQ4_XS 136 B per 256 weights):
+"""The reference's GGUF expert formats on the GPU (llama.cpp IQ2_S 82 B, IQ3_S 110 B, IQ4_XS 136 B per 256 weights:
+the GLM-5.3-Flash tables; Q2_K 84 B and Q3_K 110 B: its MTP layer):
   * dequant_rows: the counterpart of iqquant.dequant_rows (engine/glm53/iqquant.py:230-235) through
     cbmoe_iq_dequant, bit for bit the reference's fp32 values;
   * pack_layer / apply: routed experts straight from the raw GGUF tables (ResidentFetch.apply with IQ qtypes,
@@ -14,7 +14,8 @@ import torch
 
 from ._lib import IqExperts, check, lib, ptr, require_cuda, stream_handle
 
-GGML_TYPE = {"IQ3_S": 21, "IQ2_S": 22, "IQ4_XS": 23}
+GGML_TYPE = {"Q2_K": 10, "Q3_K": 11, "IQ3_S": 21, "IQ2_S": 22, "IQ4_XS": 23}
+NO_TABLE = ("Q2_K", "Q3_K")   # the K-quants of the reference's MTP layer need no lookup table
 QK_K = 256
 _tables = {}
 
@@ -33,7 +34,10 @@ def _host_table(qtype):
 
 
 def table(qtype, device):
-    """The format's fp32 lookup table on `device` (gguf-py's grid / IQ4_NL levels), shape checked by the library."""
+    """The format's fp32 lookup table on `device` (gguf-py's grid / IQ4_NL levels), shape checked by the library;
+    None for the K-quants."""
+    if qtype in NO_TABLE:
+        return None
     key = (qtype, torch.device(device))
     t = _tables.get(key)
     if t is None:
@@ -80,9 +84,10 @@ def pack_layer(gate, up, down, qtypes, E, H, I):
 
 def experts_struct(p):
     q, t = p["qtypes"], p["tables"]
+    tp = {k: (None if v is None else v.data_ptr()) for k, v in t.items()}
     return IqExperts(p["E"], p["H"], p["I"], GGML_TYPE[q["gate_q"]], GGML_TYPE[q["up_q"]], GGML_TYPE[q["down_q"]],
                      p["gate_q"].data_ptr(), p["up_q"].data_ptr(), p["down_q"].data_ptr(),
-                     t["gate_q"].data_ptr(), t["up_q"].data_ptr(), t["down_q"].data_ptr())
+                     tp["gate_q"], tp["up_q"], tp["down_q"])
 
 
 _ws = {}

@@ -1,85 +1,20 @@
-// llama.cpp IQ expert formats (the reference's real GLM-5.3-Flash tables): dequant of raw GGUF blocks on the GPU.
-// Counterpart of the reference's iqquant.dequant_rows / dequant_iq2_s / dequant_iq3_s / dequant_iq4_xs
-// (engine/glm53/iqquant.py:108-146, 230-235) and planes.dequant_planes (planes.py:183-196), in fp32, bit for bit:
-// the same products in the same order, each rounded once (no fused multiply-add).
-//
-// One warp per 256-weight block, lane l producing weights 8l .. 8l+7 (two 16-byte stores):
-//   IQ2_S  (82 B)  lane l = group l of 8: 10-bit grid index (qs byte | 2 bits of qh), sign byte, 4-bit scale of
-//                  its 16 weights; w = ((d * (0.5 + s)) * 0.25) * grid[idx][k], negated where the sign bit is set.
-//   IQ3_S  (110 B) lane l = groups 2l, 2l+1 of 4: 9-bit index (qs byte | 1 bit of qh), sign byte l, 4-bit scale of
-//                  its 32 weights; w = (d * (1 + 2s)) * grid[idx][k], sign as above.
-//   IQ4_XS (136 B) lane l = 8 weights of sub-block l/4 (32 weights): low nibbles for the first 16, high for the rest;
-//                  w = (d * (scale - 32)) * kvalues[nibble], scale = 4 low bits | 2 high bits << 4.
-// The lookup tables are the caller's (fp32, from gguf-py's grids): IQ2_S [1024][8], IQ3_S [512][4], IQ4_XS [16].
+// The reference's GGUF expert formats (llama.cpp IQ2_S / IQ3_S / IQ4_XS, and Q2_K / Q3_K of its MTP layer): dequant
+// of raw GGUF blocks on the GPU and the routed experts straight from those tables. The per-lane arithmetic is
+// iqlane.cuh (shared with a host test harness).
+// Counterpart of the reference's iqquant.dequant_rows and dequant_* (engine/glm53/iqquant.py:108-146, 200-235) and
+// planes.dequant_planes (planes.py:183-196), in fp32, bit for bit: the same products in the same order, each rounded
+// once (no fused multiply-add). One warp per 256-weight block, lane l producing weights 8l .. 8l+7 (iq_lane8, two
+// 16-byte stores). The lookup tables are the caller's (fp32, gguf-py's grids): IQ2_S [1024][8], IQ3_S [512][4],
+// IQ4_XS [16]; the K-quants need none.
 #include <cuda_fp16.h>
 
+#include "iqlane.cuh"
 #include "layer.cuh"
 #include "profile.cuh"
 
 namespace cbmoe {
 
 namespace {
-
-template <int T>
-struct IqFmt;
-template <>
-struct IqFmt<CBMOE_GGML_IQ2_S> {
-  static constexpr int kBytes = 82, kEntries = 1024, kWidth = 8;
-};
-template <>
-struct IqFmt<CBMOE_GGML_IQ3_S> {
-  static constexpr int kBytes = 110, kEntries = 512, kWidth = 4;
-};
-template <>
-struct IqFmt<CBMOE_GGML_IQ4_XS> {
-  static constexpr int kBytes = 136, kEntries = 16, kWidth = 1;
-};
-
-__device__ __forceinline__ float f16_at(const uint8_t* p) {
-  const unsigned short bits = (unsigned short)(p[0] | (p[1] << 8));
-  return __half2float(__ushort_as_half(bits));
-}
-
-__device__ __forceinline__ float with_sign(float v, unsigned sign_byte, int k) {
-  return ((sign_byte >> k) & 1u) ? -v : v;
-}
-
-// Weights 8*lane .. 8*lane+7 of one 256-weight block (see the file comment), fp32, products rounded once.
-template <int T>
-__device__ __forceinline__ void iq_lane8(const uint8_t* __restrict__ blk, int lane, const float* table,
-                                         float (&v)[8]) {
-  const float d = f16_at(blk);
-  if constexpr (T == CBMOE_GGML_IQ2_S) {
-    const int g = lane;
-    const int idx = blk[2 + g] | (((blk[66 + g / 4] >> (2 * (g % 4))) & 3) << 8);
-    const int s = (blk[74 + g / 4] >> (4 * ((g / 2) % 2))) & 15;
-    const unsigned sg = blk[34 + g];
-    const float db = __fmul_rn(__fmul_rn(d, 0.5f + (float)s), 0.25f);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = with_sign(__fmul_rn(db, table[idx * 8 + k]), sg, k);
-  } else if constexpr (T == CBMOE_GGML_IQ3_S) {
-    const int m = lane / 4;   // 32-weight scale group
-    const int s = (blk[106 + m / 2] >> (4 * (m % 2))) & 15;
-    const float db = __fmul_rn(d, (float)(1 + 2 * s));
-    const unsigned sg = blk[74 + lane];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int G = 2 * lane + h;
-      const int idx = blk[2 + G] | (((blk[66 + G / 8] >> (G % 8)) & 1) << 8);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) v[4 * h + q] = with_sign(__fmul_rn(db, table[idx * 4 + q]), sg, 4 * h + q);
-    }
-  } else {
-    const int i = lane / 4, q = (lane % 4) * 8;   // sub-block, first position inside it
-    const int sh = blk[2] | (blk[3] << 8);
-    const int sc = (((blk[4 + i / 2] >> (4 * (i % 2))) & 15) | (((sh >> (2 * i)) & 3) << 4)) - 32;
-    const float dl = __fmul_rn(d, (float)sc);
-    const uint8_t* qs = blk + 8 + 16 * i + (q & 15);
-    const int shift = q >= 16 ? 4 : 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(dl, table[(qs[j] >> shift) & 15]);
-  }
-}
 
 template <int T>
 __global__ void iq_dequant_kernel(const uint8_t* __restrict__ blocks, long long n_blocks,
@@ -146,8 +81,8 @@ __device__ __forceinline__ void bf16x8(const uint4& q, float (&f)[8]) {
 template <int T, int H_IN>
 __global__ void __launch_bounds__(256) iq_matvec_kernel(const IqMatParams p) {
   constexpr int BB = IqFmt<T>::kBytes;
-  constexpr int TAB = IqFmt<T>::kEntries * IqFmt<T>::kWidth;
-  __shared__ float tab[TAB];
+  constexpr int TAB = IqFmt<T>::kEntries * IqFmt<T>::kWidth;   // 0: no lookup table (K-quants)
+  __shared__ float tab[TAB > 0 ? TAB : 1];
   for (int i = threadIdx.x; i < TAB; i += blockDim.x) tab[i] = p.table[i];
   __syncthreads();
   const int lane = threadIdx.x & 31;
@@ -215,7 +150,9 @@ int launch_iq_matvec(int type, const IqMatParams& p, long long max_items, int ki
   switch (type) {
     case CBMOE_GGML_IQ2_S: iq_matvec_kernel<CBMOE_GGML_IQ2_S, H_IN><<<(int)grid, 256, 0, s>>>(p); break;
     case CBMOE_GGML_IQ3_S: iq_matvec_kernel<CBMOE_GGML_IQ3_S, H_IN><<<(int)grid, 256, 0, s>>>(p); break;
-    default: iq_matvec_kernel<CBMOE_GGML_IQ4_XS, H_IN><<<(int)grid, 256, 0, s>>>(p); break;
+    case CBMOE_GGML_IQ4_XS: iq_matvec_kernel<CBMOE_GGML_IQ4_XS, H_IN><<<(int)grid, 256, 0, s>>>(p); break;
+    case CBMOE_GGML_Q2_K: iq_matvec_kernel<CBMOE_GGML_Q2_K, H_IN><<<(int)grid, 256, 0, s>>>(p); break;
+    default: iq_matvec_kernel<CBMOE_GGML_Q3_K, H_IN><<<(int)grid, 256, 0, s>>>(p); break;
   }
   prof_end(kind, s);
   CBMOE_CUDA_TRY(cudaGetLastError());
@@ -241,11 +178,14 @@ IqWorkspace iq_workspace(const cbmoe_iq_experts* ex, int N, int k) {
   return w;
 }
 
+bool iq_has_table(int t) { return t == CBMOE_GGML_IQ2_S || t == CBMOE_GGML_IQ3_S || t == CBMOE_GGML_IQ4_XS; }
+
 bool iq_experts_ok(const cbmoe_iq_experts* ex) {
   auto ok_type = [](int t) { return cbmoe_iq_block_bytes(t) != 0; };
   return ex && ex->E > 0 && ex->E <= 1024 && ex->H > 0 && ex->I > 0 && ex->H % 256 == 0 && ex->I % 256 == 0 &&
          ok_type(ex->gate_type) && ok_type(ex->up_type) && ok_type(ex->down_type) && ex->gate && ex->up &&
-         ex->down && ex->gate_table && ex->up_table && ex->down_table;
+         ex->down && (ex->gate_table || !iq_has_table(ex->gate_type)) &&
+         (ex->up_table || !iq_has_table(ex->up_type)) && (ex->down_table || !iq_has_table(ex->down_type));
 }
 
 }  // namespace
@@ -325,6 +265,8 @@ extern "C" size_t cbmoe_iq_block_bytes(int ggml_type) {
     case CBMOE_GGML_IQ2_S: return IqFmt<CBMOE_GGML_IQ2_S>::kBytes;
     case CBMOE_GGML_IQ3_S: return IqFmt<CBMOE_GGML_IQ3_S>::kBytes;
     case CBMOE_GGML_IQ4_XS: return IqFmt<CBMOE_GGML_IQ4_XS>::kBytes;
+    case CBMOE_GGML_Q2_K: return IqFmt<CBMOE_GGML_Q2_K>::kBytes;
+    case CBMOE_GGML_Q3_K: return IqFmt<CBMOE_GGML_Q3_K>::kBytes;
     default: return 0;
   }
 }
@@ -335,6 +277,8 @@ extern "C" int cbmoe_iq_table_shape(int ggml_type, int* entries, int* width) {
     case CBMOE_GGML_IQ2_S: *entries = IqFmt<CBMOE_GGML_IQ2_S>::kEntries; *width = IqFmt<CBMOE_GGML_IQ2_S>::kWidth; break;
     case CBMOE_GGML_IQ3_S: *entries = IqFmt<CBMOE_GGML_IQ3_S>::kEntries; *width = IqFmt<CBMOE_GGML_IQ3_S>::kWidth; break;
     case CBMOE_GGML_IQ4_XS: *entries = IqFmt<CBMOE_GGML_IQ4_XS>::kEntries; *width = IqFmt<CBMOE_GGML_IQ4_XS>::kWidth; break;
+    case CBMOE_GGML_Q2_K:
+    case CBMOE_GGML_Q3_K: *entries = 0; *width = 0; break;
     default: return CBMOE_ERR_UNSUPPORTED;
   }
   return CBMOE_OK;
@@ -345,12 +289,14 @@ extern "C" int cbmoe_iq_dequant(int ggml_type, const void* blocks, long long n_b
   if (cbmoe_iq_block_bytes(ggml_type) == 0) return CBMOE_ERR_UNSUPPORTED;
   if (n_blocks < 0) return CBMOE_ERR_INVALID;
   if (n_blocks == 0) return CBMOE_OK;
-  if (!blocks || !table || !out || (reinterpret_cast<uintptr_t>(out) & 15) ||
+  if (!blocks || !out || (reinterpret_cast<uintptr_t>(out) & 15) || (iq_has_table(ggml_type) && !table) ||
       (reinterpret_cast<uintptr_t>(table) & 3))
     return CBMOE_ERR_INVALID;
   switch (ggml_type) {
     case CBMOE_GGML_IQ2_S: return launch_iq<CBMOE_GGML_IQ2_S>(blocks, n_blocks, table, out, stream);
     case CBMOE_GGML_IQ3_S: return launch_iq<CBMOE_GGML_IQ3_S>(blocks, n_blocks, table, out, stream);
-    default: return launch_iq<CBMOE_GGML_IQ4_XS>(blocks, n_blocks, table, out, stream);
+    case CBMOE_GGML_IQ4_XS: return launch_iq<CBMOE_GGML_IQ4_XS>(blocks, n_blocks, table, out, stream);
+    case CBMOE_GGML_Q2_K: return launch_iq<CBMOE_GGML_Q2_K>(blocks, n_blocks, table, out, stream);
+    default: return launch_iq<CBMOE_GGML_Q3_K>(blocks, n_blocks, table, out, stream);
   }
 }

@@ -1,4 +1,5 @@
-"""llama.cpp IQ expert formats: CPU restatement (test infrastructure, see oracle/__init__.py).
+"""The reference's GGUF expert formats (llama.cpp IQ2_S / IQ3_S / IQ4_XS, and Q2_K / Q3_K of its MTP layer):
+CPU restatement (test infrastructure, see oracle/__init__.py).
 
 The reference's GLM-5.3-Flash tables use llama.cpp's codebook ("IQ") quantizations; its dequant is
 launcher/glm53-flash/engine/glm53/iqquant.py (dequant_iq2_s :108-121, dequant_iq3_s :124-134, dequant_iq4_xs
@@ -22,8 +23,9 @@ All arithmetic in fp32 in this order, matching gguf-py and the reference bit for
 import numpy as np
 
 QK = 256
-BLOCK_BYTES = {"IQ2_S": 82, "IQ3_S": 110, "IQ4_XS": 136}
-GGML_TYPE = {"IQ3_S": 21, "IQ2_S": 22, "IQ4_XS": 23}   # ggml_type / GGMLQuantizationType numbers
+BLOCK_BYTES = {"IQ2_S": 82, "IQ3_S": 110, "IQ4_XS": 136, "Q2_K": 84, "Q3_K": 110}
+GGML_TYPE = {"Q2_K": 10, "Q3_K": 11, "IQ3_S": 21, "IQ2_S": 22, "IQ4_XS": 23}   # ggml_type numbers
+D_OFFSET = {"IQ2_S": 0, "IQ3_S": 0, "IQ4_XS": 0, "Q2_K": 80, "Q3_K": 108}        # byte of the f16 block scale
 
 
 def tables():
@@ -35,6 +37,7 @@ def tables():
         cls.init_grid()
         out[qt] = np.asarray(cls.grid, np.float32).reshape(cls.grid_shape)
     out["IQ4_XS"] = np.asarray(gq.IQ4_NL.kvalues, np.float32)
+    out["Q2_K"] = out["Q3_K"] = None                                          # no lookup table
     return out
 
 
@@ -89,7 +92,44 @@ def dequant_iq4_xs(blk, kvalues):
     return (dl[:, :, None] * kvalues[nib]).reshape(nb, QK)
 
 
-DEQUANT = {"IQ2_S": dequant_iq2_s, "IQ3_S": dequant_iq3_s, "IQ4_XS": dequant_iq4_xs}
+def dequant_q2_k(blk, _table=None):
+    """Q2_K (84 B: scales[16] | qs[64] | d f16 | dmin f16), the reference's MTP-layer experts (iqquant.py:200-212).
+    Weight 128n + 32s + l = (qs[32n + l] >> 2s) & 3, scale byte 8n + 2s + l // 16 (low nibble x d, high nibble x
+    dmin): w = (d * sc) * q - dmin * m, each product and the difference rounded to fp32."""
+    nb = blk.shape[0]
+    sc = blk[:, 0:16]
+    d = np.ascontiguousarray(blk[:, 80:82]).view(np.float16).astype(np.float32)[:, 0]
+    dmin = np.ascontiguousarray(blk[:, 82:84]).view(np.float16).astype(np.float32)[:, 0]
+    dl = (d[:, None] * (sc & 15).astype(np.float32))[:, :, None]            # [nb, 16, 1]
+    ml = (dmin[:, None] * (sc >> 4).astype(np.float32))[:, :, None]
+    q = (blk[:, 16:80].reshape(nb, 2, 1, 32) >> np.array([0, 2, 4, 6], np.uint8).reshape(1, 1, 4, 1)) & 3
+    q = q.reshape(nb, 16, 16).astype(np.float32)
+    return (dl * q - ml).reshape(nb, QK)
+
+
+def q3k_scales(sc):
+    """The 16 six-bit scales of a Q3_K block's 12 bytes: scale m = (low nibble m // 8 of byte m % 8) | (2 bits
+    2 (m // 4) of byte 8 + m % 4) << 4."""
+    nb = sc.shape[0]
+    lo = (sc[:, 0:8].reshape(nb, 1, 8) >> np.array([0, 4], np.uint8).reshape(1, 2, 1)).reshape(nb, 16) & 15
+    hi = (sc[:, 8:12].reshape(nb, 1, 4) >> np.array([0, 2, 4, 6], np.uint8).reshape(1, 4, 1)).reshape(nb, 16) & 3
+    return (lo | (hi << 4)).astype(np.int32)
+
+
+def dequant_q3_k(blk, _table=None):
+    """Q3_K (110 B: hmask[32] | qs[64] | scales[12] | d f16), iqquant.py:215-226. Weight 128n + 32s + l:
+    q = ((qs[32 + 32n + l] >> 2s) & 3) - 4 unless bit 4n + s of hmask[l] is set; w = (d * (scale - 32)) * q."""
+    nb = blk.shape[0]
+    d = np.ascontiguousarray(blk[:, 108:110]).view(np.float16).astype(np.float32)[:, 0]
+    dl = (d[:, None] * (q3k_scales(blk[:, 96:108]) - 32).astype(np.float32))[:, :, None]   # [nb, 16, 1]
+    ql = (blk[:, 32:96].reshape(nb, 2, 1, 32) >> np.array([0, 2, 4, 6], np.uint8).reshape(1, 1, 4, 1)) & 3
+    qh = (blk[:, 0:32].reshape(nb, 1, 32) >> np.arange(8, dtype=np.uint8).reshape(1, 8, 1)) & 1
+    q = ql.reshape(nb, 16, 16).astype(np.int32) - 4 * (1 - qh.reshape(nb, 16, 16).astype(np.int32))
+    return (dl * q.astype(np.float32)).reshape(nb, QK)
+
+
+DEQUANT = {"IQ2_S": dequant_iq2_s, "IQ3_S": dequant_iq3_s, "IQ4_XS": dequant_iq4_xs, "Q2_K": dequant_q2_k,
+           "Q3_K": dequant_q3_k}
 
 
 def dequant_rows(raw, qtype, ne0, tabs=None):
@@ -100,10 +140,14 @@ def dequant_rows(raw, qtype, ne0, tabs=None):
 
 
 def random_blocks(rng, n, qtype, dmin=1e-3, dmax=2e-2):
-    """n random blocks (uint8 [n, block bytes]) with a positive f16 block scale in [dmin, dmax]."""
-    bb = BLOCK_BYTES[qtype]
+    """n random blocks (uint8 [n, block bytes]) with a positive f16 block scale in [dmin, dmax] (Q2_K: also its
+    f16 min scale, a tenth of that)."""
+    bb, off = BLOCK_BYTES[qtype], D_OFFSET[qtype]
     b = rng.integers(0, 256, (n, bb), dtype=np.uint8)
-    b[:, 0:2] = np.frombuffer(rng.uniform(dmin, dmax, n).astype(np.float16).tobytes(), np.uint8).reshape(n, 2)
+    b[:, off:off + 2] = np.frombuffer(rng.uniform(dmin, dmax, n).astype(np.float16).tobytes(), np.uint8).reshape(n, 2)
+    if qtype == "Q2_K":
+        b[:, 82:84] = np.frombuffer(rng.uniform(dmin / 10, dmax / 10, n).astype(np.float16).tobytes(),
+                                    np.uint8).reshape(n, 2)
     return b
 
 

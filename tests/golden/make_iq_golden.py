@@ -6,7 +6,8 @@ make_golden.py) and gguf-py installed:
 Nothing at test time reads the reference; the tests read the .npz written here (and gguf-py, which is installed).
 
 Executed reference functions (launcher/glm53-flash/engine/glm53/iqquant.py): dequant_iq2_s, dequant_iq3_s,
-dequant_iq4_xs and the helpers they call (_f16, _u16, _bits8, _nibbles, _signs_from_bits, _kv16, lookup with
+dequant_iq4_xs, dequant_q2_k, dequant_q3_k and the helpers they call (_f16, _u16, _bits8, _nibbles,
+_signs_from_bits, _kv16, _f16_at, _kq_layout, q3k_scales, lookup with
 LOOKUP_IMPL = "take", which the reference's tests hold equal to its select-tree lookup), on the NumPy stand-in
 for jax of make_golden.py plus `jax.lax.bitcast_convert_type`. The grid tables come from the reference's own
 iq_grids_data.py. Inputs:
@@ -14,7 +15,7 @@ iq_grids_data.py. Inputs:
     gguf_samples.json): IQ2_S 2 x 4096 (blk.3.ffn_gate_exps), IQ3_S 4 x 2048 (blk.3.ffn_down_exps), IQ4_XS 4 x 2048
     (blk.11.ffn_down_exps), stored here as raw bytes with the reference's output;
   * 16 random blocks per format (seeded; block scale d a positive f16 in [1e-3, 2e-2] as in the reference's
-    test_random_blocks_match_gguf_py).
+    test_random_blocks_match_gguf_py; Q2_K/Q3_K, which have no sample, only these).
 Every output is also checked against gguf-py's dequantize (the reference's own oracle) before it is written.
 """
 import importlib.util
@@ -30,6 +31,7 @@ sys.path.insert(0, HERE)
 import make_golden as mg  # noqa: E402  (the NumPy stand-in for jax and ref_function)
 
 BLOCK_BYTES = {"IQ2_S": 82, "IQ3_S": 110, "IQ4_XS": 136}
+KQUANT_BYTES = {"Q2_K": 84, "Q3_K": 110}   # the MTP layer's formats: no GGUF sample in the reference, random blocks
 
 
 def _bitcast(x, dtype):
@@ -61,7 +63,12 @@ def reference_dequant():
           "KVALUES_IQ4NL": np.asarray(g["kvalues_iq4nl"]), "_TREES": {}}
     for name in ("_u16", "_u32", "_f16", "_bits8", "_nibbles", "_signs_from_bits", "_kv16", "lookup"):
         ns[name] = mg.ref_function("iqquant.py", name, extra=ns)
-    return {qt: mg.ref_function("iqquant.py", f"dequant_{qt.lower()}", extra=ns) for qt in BLOCK_BYTES}
+    ns["q3k_scales"] = mg.ref_function("iqquant.py", "q3k_scales", extra=ns)
+    ns["_f16_at"] = mg.ref_function("iqquant.py", "_f16_at", extra=ns)
+    ns["_kq_layout"] = mg.ref_function("iqquant.py", "_kq_layout", extra=ns)
+    out = {qt: mg.ref_function("iqquant.py", f"dequant_{qt.lower()}", extra=ns) for qt in BLOCK_BYTES}
+    out.update({qt: mg.ref_function("iqquant.py", f"dequant_{qt.lower()}", extra=ns) for qt in KQUANT_BYTES})
+    return out
 
 
 def gguf_dequant(raw, qt):
@@ -89,6 +96,17 @@ def main():
         d = rng.uniform(1e-3, 2e-2, 16).astype(np.float16)
         rb[:, 0:2] = np.frombuffer(d.tobytes(), np.uint8).reshape(16, 2)
         rref = np.asarray(deq[qt](mg.J(rb)), np.float32).reshape(16, 256)
+        np.testing.assert_array_equal(rref, gguf_dequant(rb, qt).reshape(16, 256))
+        out.update({f"{qt}_rand_raw": rb, f"{qt}_rand_ref": rref})
+    for qt, bb in KQUANT_BYTES.items():
+        off = {"Q2_K": 80, "Q3_K": 108}[qt]
+        rb = rng.integers(0, 256, (16, bb), dtype=np.uint8)
+        rb[:, off:off + 2] = np.frombuffer(rng.uniform(1e-3, 2e-2, 16).astype(np.float16).tobytes(),
+                                           np.uint8).reshape(16, 2)
+        if qt == "Q2_K":
+            rb[:, 82:84] = np.frombuffer(rng.uniform(1e-4, 2e-3, 16).astype(np.float16).tobytes(),
+                                         np.uint8).reshape(16, 2)
+        rref = np.asarray(deq[qt](mg.J(rb.reshape(16, 1, bb))), np.float32).reshape(16, 256)
         np.testing.assert_array_equal(rref, gguf_dequant(rb, qt).reshape(16, 256))
         out.update({f"{qt}_rand_raw": rb, f"{qt}_rand_ref": rref})
     np.savez_compressed(os.path.join(HERE, "iq_samples.npz"), **out)

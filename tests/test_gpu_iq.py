@@ -13,6 +13,7 @@ from oracle import iq as oiq
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "iq_samples.npz")
 QTYPES = list(oiq.BLOCK_BYTES)
+SAMPLED = ["IQ2_S", "IQ3_S", "IQ4_XS"]
 
 
 @pytest.fixture(scope="module")
@@ -24,7 +25,7 @@ def cbmoe():
     return c
 
 
-@pytest.mark.parametrize("qt", QTYPES)
+@pytest.mark.parametrize("qt", SAMPLED)
 def test_reference_samples_bit_exact(cbmoe, qt):
     f = np.load(GOLDEN)
     raw = torch.from_numpy(f[f"{qt}_raw"].copy()).cuda()
@@ -41,7 +42,9 @@ def test_random_blocks_bit_exact(cbmoe, qt, n_blocks):
     rng = np.random.default_rng(n_blocks * 3 + len(qt))
     blk = oiq.random_blocks(rng, n_blocks, qt)
     if n_blocks >= 8:   # zero, negative and subnormal block scales
-        blk[:3, 0:2] = np.frombuffer(np.array([0.0, -0.02, 6.0e-5], np.float16).tobytes(), np.uint8).reshape(3, 2)
+        off = oiq.D_OFFSET[qt]
+        blk[:3, off:off + 2] = np.frombuffer(np.array([0.0, -0.02, 6.0e-5], np.float16).tobytes(),
+                                             np.uint8).reshape(3, 2)
     want = oiq.DEQUANT[qt](blk, oiq.tables()[qt])
     got = cbmoe.iq.dequant_rows(torch.from_numpy(blk.reshape(-1)).cuda(), qt, 256).cpu().numpy()
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
@@ -62,7 +65,7 @@ def test_rejects_bad_arguments(cbmoe):
 
 # ---------------------------------------------------------------------------------- routed experts on IQ tables
 @pytest.mark.parametrize("types", [("IQ2_S", "IQ2_S", "IQ3_S"), ("IQ4_XS", "IQ4_XS", "IQ4_XS"),
-                                   ("IQ3_S", "IQ2_S", "IQ4_XS")])
+                                   ("IQ3_S", "IQ2_S", "IQ4_XS"), ("Q2_K", "Q2_K", "Q3_K")])
 @pytest.mark.parametrize("N,k,E", [(1, 8, 16), (8, 8, 24), (37, 4, 8)])
 def test_iq_experts_apply(cbmoe, types, N, k, E):
     """ResidentFetch.apply over raw GGUF IQ tables (per-matrix formats, as the reference's qtypes) against the

@@ -1,4 +1,5 @@
-"""The IQ-format oracle (oracle/iq.py) pinned against the reference (CPU only).
+"""The GGUF-format oracle (oracle/iq.py: IQ2_S / IQ3_S / IQ4_XS, Q2_K / Q3_K) pinned against the reference (CPU
+only).
 
 The reference's own IQ dequant (iqquant.py, executed on its GGUF samples and on random blocks by
 tests/golden/make_iq_golden.py) and gguf-py 0.19.0 (the reference's third-party oracle,
@@ -13,6 +14,7 @@ from oracle import iq
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "iq_samples.npz")
 QTYPES = list(iq.BLOCK_BYTES)
+SAMPLED = ["IQ2_S", "IQ3_S", "IQ4_XS"]   # the formats with a real GGUF slice in the reference's tests
 
 
 @pytest.fixture(scope="module")
@@ -25,7 +27,7 @@ def golden():
     return np.load(GOLDEN)
 
 
-@pytest.mark.parametrize("qt", QTYPES)
+@pytest.mark.parametrize("qt", SAMPLED)
 def test_reference_gguf_samples_bit_exact(qt, tabs, golden):
     """The real GLM-5.3-Flash tensor slices of the reference's tests, against the reference's own output."""
     got = iq.dequant_rows(golden[f"{qt}_raw"], qt, int(golden[f"{qt}_ne0"]), tabs)
@@ -46,7 +48,8 @@ def test_random_blocks_match_gguf_py(qt, tabs):
     from gguf import GGMLQuantizationType as T
     rng = np.random.default_rng(7)
     blk = iq.random_blocks(rng, 256, qt)
-    blk[:3, 0:2] = np.frombuffer(np.array([0.0, -0.02, 6.0e-5], np.float16).tobytes(), np.uint8).reshape(3, 2)
+    off = iq.D_OFFSET[qt]
+    blk[:3, off:off + 2] = np.frombuffer(np.array([0.0, -0.02, 6.0e-5], np.float16).tobytes(), np.uint8).reshape(3, 2)
     want = gq.dequantize(blk.reshape(-1), getattr(T, qt)).reshape(256, 256)
     assert np.array_equal(iq.DEQUANT[qt](blk, tabs[qt]), want)
 
