@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this folder by EXECUTING the reference's own functions.
 
-Run in a container that has the reference checkout (read-only) at REF (default below, or $CBMOE_REFERENCE):
-    python tests/golden/make_golden.py
+Run where the reference checkout (read-only) is available, naming its root in $CBMOE_REFERENCE:
+    CBMOE_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 Nothing at test time reads the reference; the tests only read the .npz written here.
 
 JAX is not installed here, so the reference functions run on a NumPy-backed stand-in for the few `jax`,
@@ -34,7 +34,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 from oracle import cb3  # noqa: E402  (only for generating packed CB3 inputs)
 
-REF = os.environ.get("CBMOE_REFERENCE", "/root/reference")
+REF = os.environ.get("CBMOE_REFERENCE", "")
 ENGINE = os.path.join(REF, "launcher", "glm53-flash", "engine", "glm53")
 
 
@@ -236,7 +236,7 @@ def gen_compositions():
 
 
 if __name__ == "__main__":
-    assert os.path.isdir(ENGINE), f"reference engine not found at {ENGINE}"
+    assert os.path.isdir(ENGINE), f"reference engine not found at {ENGINE!r}: set CBMOE_REFERENCE"
     gen_plans()
     gen_swiglu()
     gen_quant8()

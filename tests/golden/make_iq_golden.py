@@ -1,8 +1,8 @@
 """Generate iq_samples.npz in this folder by EXECUTING the reference's IQ dequant (iqquant.py) on its own GGUF samples.
 
-Run in a container that has the reference checkout (read-only) at REF ($CBMOE_REFERENCE, default as in
-make_golden.py) and gguf-py installed:
-    python tests/golden/make_iq_golden.py
+Run where the reference checkout (read-only) is available, naming its root in $CBMOE_REFERENCE, with gguf-py
+installed:
+    CBMOE_REFERENCE=<reference checkout> python tests/golden/make_iq_golden.py
 Nothing at test time reads the reference; the tests read the .npz written here (and gguf-py, which is installed).
 
 Executed reference functions (launcher/glm53-flash/engine/glm53/iqquant.py): dequant_iq2_s, dequant_iq3_s,

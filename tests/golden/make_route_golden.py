@@ -1,8 +1,7 @@
 """Generate route.npz in this folder by EXECUTING the reference's router, moe_route (engine/glm53/model.py:798-808).
 
-Run in a container that has the reference checkout (read-only) at REF ($CBMOE_REFERENCE, default as in
-make_golden.py):
-    python tests/golden/make_route_golden.py
+Run where the reference checkout (read-only) is available, naming its root in $CBMOE_REFERENCE:
+    CBMOE_REFERENCE=<reference checkout> python tests/golden/make_route_golden.py
 The function runs on make_golden.py's NumPy stand-in for jax, plus `lax.top_k` as a stable descending sort (the
 largest values first, the lower index first among equal ones, as XLA's top_k orders them) and `jax.nn.sigmoid`.
 Inputs: bf16-exact x [16, 256] and router weights [256, 160], a bias [160] (the e_score_correction_bias role),
