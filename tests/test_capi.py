@@ -88,3 +88,15 @@ def test_iq_and_route_host_side(L):
     assert L.cbmoe_route(None, 1, 64, None, None, 300, 8, 1, 1.0, None, None, None) == -1   # E > 256
     assert L.cbmoe_route(None, 1, 64, None, None, 16, 17, 1, 1.0, None, None, None) == -1   # k > E
     assert L.cbmoe_route(None, 0, 64, None, None, 16, 8, 1, 1.0, None, None, None) == 0     # nothing to do
+
+
+def test_workspace_queries_without_gpu(L):
+    """Workspace sizes of every path are host arithmetic: positive, growing with the batch, and the tcgen05 decode
+    path (which adds the gathered token rows) larger than the mma.sync one at the same shape."""
+    from cbmoe._lib import Experts
+    ex = Experts(160, 5120, 1536, 16, 16, 16, 16)
+    dec = [L.cbmoe_workspace_bytes(ctypes.byref(ex), n, 8, 1) for n in (1, 8, 64)]
+    assert all(v > 0 for v in dec) and dec[0] <= dec[1] <= dec[2]
+    assert L.cbmoe_workspace_bytes(ctypes.byref(ex), 8, 8, 3) > dec[1]             # CBMOE_PATH_DECODE_TC
+    assert L.cbmoe_workspace_bytes(ctypes.byref(ex), 4096, 8, 2) > dec[2]          # grouped, config 3
+    assert L.cbmoe_ep_workspace_bytes(ctypes.byref(Experts(20, 5120, 1536, 16, 16, 16, 16)), 32, 8, 8, 64, 0) > 0
