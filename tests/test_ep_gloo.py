@@ -86,3 +86,20 @@ def test_ep_protocol_two_ranks(cap):
             assert err < 1e-6, (rank, err)
         else:                                           # a too-small capacity drops slots (flagged, not fatal)
             assert cap == 5 and err > 0
+
+
+def test_ep_protocol_four_ranks():
+    """The same protocol over 4 ranks (2 experts and 3 tokens per rank): the bookkeeping the 4- and 8-GPU runs use."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 4, port, 12, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+        assert p.exitcode == 0, "rank failed"
+    res = [q.get(timeout=10) for _ in procs]
+    assert sorted(r for r, _, _ in res) == [0, 1, 2, 3]
+    for rank, err, dropped in res:
+        assert dropped == 0 and err < 1e-6, (rank, err, dropped)
