@@ -5,7 +5,8 @@
  *   - returns CBMOE_OK (0) or a negative CBMOE_ERR_* status; never throws, never aborts;
  *   - pointer arguments are DEVICE pointers unless the name ends in _host;
  *   - work is enqueued on `stream` (stream-ordered, asynchronous); nothing synchronizes unless documented;
- *   - tables and buffers are owned by the caller; the library allocates no device memory on any path;
+ *   - tables and buffers are owned by the caller; no compute path allocates device memory (the set-up calls
+ *     cbmoe_ep_comm_init and cbmoe_ep_peer_init do, and cbmoe_ep_peer_destroy frees what the latter took);
  *   - bf16 tensors are passed as uint16_t bit patterns;
  *   - kernels never trap: a device-side problem (a wait that ran out, an expert id out of range) sets a bit
  *     that cbmoe_device_errors() reports.
@@ -37,11 +38,6 @@ extern "C" {
 #define CBMOE_PATH_AUTO 0          /* decode kernel for small batches, grouped tensor-core GEMM otherwise */
 #define CBMOE_PATH_DECODE 1        /* fused dequant matvec (resident.py:110-120 `_apply_kernel`) */
 #define CBMOE_PATH_GROUPED 2       /* grouped dequant GEMM (resident.py:144-165 `_apply_ragged_kernel`) */
-#define CBMOE_PATH_DECODE_TC 3     /* the decode composition with the dequantized weights stored into TMEM and
-                                      contracted by tcgen05.mma (H, I multiples of 128). Same results as
-                                      CBMOE_PATH_DECODE within rounding; slower at every measured size on B200
-                                      (a 128x16x16 tcgen05.mma costs as long as a 128x128x16 one), kept for
-                                      comparison. Not used by CBMOE_PATH_AUTO. */
 
 /* ---------------------------------------------------------------------------------------------- library */
 int cbmoe_version(void);
@@ -85,6 +81,17 @@ int cbmoe_cb3k_repack(const uint32_t* idx0, const uint16_t* cb0, const uint32_t*
  * (planes.dequant_planes, planes.py:196-291: the bit-exactness check of layout + dequant). */
 int cbmoe_cb3k_dequant(const void* idx_k, const void* cb_k, int nmat, int E, int rows, int K, uint16_t* out,
                        cudaStream_t stream);
+/* CB8: the decode kernels' form of the CB3K codebooks (same index bits), built at load time alongside them
+ * (part of the same load-time repack, resident.py:48-60). Per row, the 8 entries as 16-bit fixed point
+ * T = rint(v 2^s) (the largest magnitude times 2^s in [2^14, 2^15)) in two byte tables, hi = T >> 8 (int8) and
+ * lo = T & 255 (uint8), and the factor 2^-s: 20 bytes per row, laid out per (expert, 64-row block) as the CB3K
+ * codebooks are. T is exact for entries within 2^7 of the row's largest magnitude and within 2^-15 of that
+ * largest magnitude below it. With these tables the decode path multiplies int8 digits on the tensor cores with
+ * exact int32 sums (activations as two base-256 digits per element with one factor per token, exact for bf16
+ * within 2^6 of the token's largest; the SwiGLU output as four, with one factor per 64 inputs), which halves the
+ * table lookups per weight of the bf16 kernels. cb_k: a CB3K codebook table. */
+size_t cbmoe_cb8_bytes(int E, int rows, int nmat);
+int cbmoe_cb8_build(const void* cb_k, int nmat, int E, int rows, void* cb8, cudaStream_t stream);
 
 /* ----------------------------------------------------------------------------------- int8 kernel layout
  * int8 weight-only leaves as quant8.quantize_array makes them (quant8.py:26-32): q int8 [K_in, rows_out]
@@ -117,6 +124,8 @@ typedef struct cbmoe_experts {
   const void* gateup_cb;
   const void* down_idx;        /* CB3K nmat = 1, rows = H, K = I */
   const void* down_cb;
+  const void* gateup_cb8;      /* CB8 tables of gateup_cb / down_cb (cbmoe_cb8_build), both or neither: with them */
+  const void* down_cb8;        /* the decode path runs the int8-digit kernels, without them the bf16 ones */
 } cbmoe_experts;
 
 typedef struct cbmoe_shared {
@@ -161,6 +170,12 @@ int cbmoe_moe_layer(const cbmoe_experts* ex, const cbmoe_shared* sh, const uint1
  * pallas_moe.py:238-307): x bf16 [N, K] -> y fp32 [N, rows]. Workspace: cbmoe_matvec_workspace_bytes. */
 size_t cbmoe_matvec_workspace_bytes(int N);
 int cbmoe_cb3_matvec(const void* idx_k, const void* cb_k, int rows, int K, const uint16_t* x, int N, float* y,
+                     void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* cbmoe_cb3_matvec on CB8 tables (cbmoe_cb8_build): the same product through the e4m3 decode kernel. The
+ * workspace (cbmoe_cb8_matvec_workspace_bytes, 16-byte aligned) holds the split activations. */
+size_t cbmoe_cb8_matvec_workspace_bytes(int N, int K);
+int cbmoe_cb8_matvec(const void* idx_k, const void* cb8, int rows, int K, const uint16_t* x, int N, float* y,
                      void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /* int8 weight-only linear (quant8.dequant_tree + the consuming dot, quant8.py:91-99): x bf16 [N, K] ->

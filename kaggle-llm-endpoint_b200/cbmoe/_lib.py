@@ -10,7 +10,7 @@ LIB_PATH = os.path.join(_HERE, "libcbmoe.so")
 
 c_int, c_float, c_size_t, c_void_p, c_int64 = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int64
 
-PATHS = {"auto": 0, "decode": 1, "grouped": 2, "decode_tc": 3}
+PATHS = {"auto": 0, "decode": 1, "grouped": 2}
 
 
 class CbmoeError(RuntimeError):
@@ -19,7 +19,7 @@ class CbmoeError(RuntimeError):
 
 class Experts(ctypes.Structure):
     _fields_ = [("E", c_int), ("H", c_int), ("I", c_int), ("gateup_idx", c_void_p), ("gateup_cb", c_void_p),
-                ("down_idx", c_void_p), ("down_cb", c_void_p)]
+                ("down_idx", c_void_p), ("down_cb", c_void_p), ("gateup_cb8", c_void_p), ("down_cb8", c_void_p)]
 
 
 class Shared(ctypes.Structure):
@@ -49,6 +49,11 @@ SIGNATURES = {
     "cbmoe_cb3k_repack": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                   c_void_p, c_void_p]),
     "cbmoe_cb3k_dequant": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "cbmoe_cb8_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "cbmoe_cb8_build": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "cbmoe_cb8_matvec_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "cbmoe_cb8_matvec": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_size_t,
+                                 c_void_p]),
     "cbmoe_w8k_bytes": (c_size_t, [c_int, c_int, c_int]),
     "cbmoe_w8k_repack": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "cbmoe_w8k_dequant": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),

@@ -15,7 +15,20 @@ import ctypes
 import torch
 import torch.distributed as dist
 
-from ._lib import PATHS, Experts, Shared, check, lib, ptr, require_cuda, stream_handle
+from ._lib import PATHS, Shared, check, lib, ptr, require_cuda, stream_handle
+from .resident import _experts_struct
+
+
+def agree_capacity(N_local, k, capacity=None, group=None):
+    """Rows per peer that every rank of `group` uses: `capacity` when given (the caller keeps it equal on every
+    rank), else the largest N_local * k over the ranks (all_reduce MAX). Ranks may hold different token counts; the
+    peer transport addresses a peer's receive rows by the capacity, so it must be one value everywhere."""
+    if capacity is not None:
+        return max(1, int(capacity))
+    dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl" else torch.device("cpu")
+    t = torch.tensor([N_local * k], dtype=torch.int64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return max(1, int(t.item()))
 
 
 class ExpertParallel:
@@ -23,6 +36,7 @@ class ExpertParallel:
     buffers set up on the first layer call, one process per GPU of one node, at most 8) or "nccl" (send/recv)."""
 
     def __init__(self, group=None, transport="peer"):
+        self.group = group
         self.rank = dist.get_rank(group)
         self.nranks = dist.get_world_size(group)
         idbuf = torch.zeros(128, dtype=torch.uint8)
@@ -89,13 +103,13 @@ class ExpertParallel:
 
     def layer(self, p, x, idx, w, limit, capacity=None, out=None, path="auto"):
         """x bf16 [N_local, H], idx int32 [N_local, k] (global expert ids), w fp32 [N_local, k] -> bf16 [N_local, H].
-        `capacity` = rows per peer in each direction (default N_local * k: never drops); `path` = kernels for the
-        received rows ("auto", "decode", "grouped")."""
+        `capacity` = rows per peer in each direction, the same on every rank (default: the largest N_local * k over
+        the ranks, agreed by one small all-reduce per call; it never drops); `path` = kernels for the received rows
+        ("auto", "decode", "grouped")."""
         require_cuda(x, idx, w)
         N, k = idx.shape
-        cap = max(1, capacity if capacity is not None else N * k)
-        ex = Experts(p["E"], p["H"], p["I"], p["gate_up_q"][0].data_ptr(), p["gate_up_q"][1].data_ptr(),
-                     p["down_q"][0].data_ptr(), p["down_q"][1].data_ptr())
+        cap = agree_capacity(N, k, capacity, self.group)
+        ex = _experts_struct(p)
         s = p["shared"]
         sh = Shared(s["gate_up_q"].data_ptr(), s["gate_s"].data_ptr(), s["up_s"].data_ptr(), s["down_q"].data_ptr(),
                     s["down_s"].data_ptr(), s["scale_axis"])

@@ -37,6 +37,28 @@ def pack_cb3(idx0, cb0, idx1=None, cb1=None):
     return idx_k, cb_k
 
 
+def build_cb8(cb_k, nmat, E, rows):
+    """CB3K codebooks -> CB8 tables (uint8: int8 hi / uint8 lo bytes + row factors) for the int8-digit decode kernels."""
+    require_cuda(cb_k)
+    out = torch.empty(lib().cbmoe_cb8_bytes(E, rows, nmat), dtype=torch.uint8, device=cb_k.device)
+    check(lib().cbmoe_cb8_build(ptr(cb_k), nmat, E, rows, ptr(out), stream_handle()), "cbmoe_cb8_build")
+    return out
+
+
+def cb8_matvec(idx_k, cb8, rows, K, x, ws=None):
+    """One matrix (expert 0 of a CB3K table) times x bf16 [N, K] -> fp32 [N, rows] on the int8-digit decode kernel.
+    `ws`: the workspace (uint8, at least cbmoe_cb8_matvec_workspace_bytes); allocated when not given."""
+    require_cuda(idx_k, cb8, x)
+    N = x.shape[0]
+    xb = x.to(torch.bfloat16).contiguous()
+    y = torch.empty((N, rows), dtype=torch.float32, device=x.device)
+    if ws is None:
+        ws = torch.empty(max(1, lib().cbmoe_cb8_matvec_workspace_bytes(N, K)), dtype=torch.uint8, device=x.device)
+    check(lib().cbmoe_cb8_matvec(ptr(idx_k), ptr(cb8), rows, K, ptr(xb), N, ptr(y), ptr(ws), ws.numel(),
+                                 stream_handle()), "cbmoe_cb8_matvec")
+    return y
+
+
 def dequant_cb3k(idx_k, cb_k, nmat, E, rows, K):
     """Kernel-layout table -> bf16 [nmat, E, rows, K] through the kernels' register dequant."""
     require_cuda(idx_k, cb_k)

@@ -19,17 +19,23 @@ from ._lib import PATHS, Experts, Shared, check, lib, ptr, require_cuda, stream_
 CB3 = "CB3"
 
 
-def pack_layer(gate, up, down, shared=None):
+def pack_layer(gate, up, down, shared=None, decode_tables="int8"):
     """Device tables of one layer from CB3 gate/up [E, I, H] and down [E, H, I] tables ((idx int32-packed uint32
     words, cb bf16) pairs on the GPU) and an optional int8 shared expert ((q [in, out] int8, s fp32) for gate, up,
-    down; scales per output column [1, out] or per input row [in, 1] as quant8.quantize_array makes them)."""
+    down; scales per output column [1, out] or per input row [in, 1] as quant8.quantize_array makes them).
+    `decode_tables`: "int8" also builds the CB8 tables, so the decode path runs the int8-digit kernels (20 bytes per row
+    more); "bf16" leaves them out (the bf16 decode kernels)."""
     (gi, gc), (ui, uc), (di, dc) = gate, up, down
     E, I, wpr = gi.shape
     H = wpr * 32 // 3
     assert di.shape[:2] == (E, H), (di.shape, E, H)
+    assert decode_tables in ("int8", "bf16"), decode_tables
     gu_idx, gu_cb = ops.pack_cb3(gi, gc, ui, uc)
     dn_idx, dn_cb = ops.pack_cb3(di, dc)
     p = {"E": E, "H": H, "I": I, "gate_up_q": (gu_idx, gu_cb), "down_q": (dn_idx, dn_cb)}
+    if decode_tables == "int8":
+        p["gate_up_cb8"] = ops.build_cb8(gu_cb, 2, E, I)
+        p["down_cb8"] = ops.build_cb8(dn_cb, 1, E, H)
     if shared is not None:
         (gq, gs), (uq, us), (dq, ds) = shared
         axis = 1 if gs.shape[0] == 1 else 0
@@ -40,8 +46,9 @@ def pack_layer(gate, up, down, shared=None):
 
 
 def _experts_struct(p):
+    cb8 = (p["gate_up_cb8"].data_ptr(), p["down_cb8"].data_ptr()) if "gate_up_cb8" in p else (None, None)
     return Experts(p["E"], p["H"], p["I"], p["gate_up_q"][0].data_ptr(), p["gate_up_q"][1].data_ptr(),
-                   p["down_q"][0].data_ptr(), p["down_q"][1].data_ptr())
+                   p["down_q"][0].data_ptr(), p["down_q"][1].data_ptr(), *cb8)
 
 
 def _shared_struct(s):
@@ -55,7 +62,7 @@ class ResidentFetch:
     Constructor knobs keep the reference's names: `qtypes` {layer: {"gate_q", "up_q", "down_q"} -> format}
     ("CB3" only here), `D`, `ml` (this GPU's intermediate size), `out_dtype` of the returned partial,
     `gather_max_rows` (slots N*k at or below which the decode kernels run; above it the grouped path), and
-    `path` to force "decode", "grouped" or "decode_tc" (the decode composition on the tcgen05 TMEM kernels)."""
+    `path` to force "decode" or "grouped"."""
 
     def __init__(self, qtypes=None, D=None, ml=None, out_dtype=torch.float32, gather_max_rows=1024, path="auto"):
         self.qtypes = qtypes or {}

@@ -44,13 +44,12 @@ int decode_nt_routed(int N, int k, int E) {
 }
 
 // Workspace of the decode path:
-//   plan | xs (Rp x H bf16: the routed rows gathered in plan order, CBMOE_PATH_DECODE_TC only) | h (Rp x 2I bf16) |
-//   y_sorted (Rp x H f32) | h_shared (N x 2I bf16) | y_shared (N x H f32) |
+//   plan | x8 (N x H/256 x 512 B: the tokens as X8 rows, CB8 tables only) | x8 factors (N f32) |
+//   h (the SwiGLU output of the routed slots: Rp x 2I bf16 (hi, lo) for the bf16 kernels, Rp x I/256 x 1040 B H8
+//   rows for the CB8 ones) | y_sorted (Rp x H f32) | h_shared (N x 2I bf16) | y_shared (N x H f32) |
 //   scheduling words: routed [gate/up tickets, down tickets, gate/up arrival counters, down arrival counters]
 //                     (zeroed by the plan kernel), shared [the same] (zeroed by a memset on the side stream) |
 //   partial sums of the tail items' pieces of the routed gate/up, routed down, shared gate/up, shared down.
-// h is [row][2I] (hi, lo per 256-input stage) for the mma.sync kernels and two planes [2][Rp][I] (hi, lo) for
-// the tcgen05 ones.
 
 // Tail items a decode launch cuts into pieces: at most half its resident grid (the kernel takes the same bound).
 int decode_tail_items(long long items) {
@@ -58,42 +57,47 @@ int decode_tail_items(long long items) {
   return (int)(items < half ? items : half);
 }
 
-DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k, long long slots_hint, int tc) {
+// Token tiles of the CB8 gate/up kernel (4 tokens each) by the average slots per expert; its passes hold 4 * nt
+// rows, and the down kernel takes the same passes in tiles of 2 slots (2 * nt tiles).
+int cb8_nt_routed(long long S, int E) { return S <= 2LL * E ? 1 : 2; }
+
+DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k, long long slots_hint, int cb8) {
   DecodeWorkspace w;
   const long long S_real = slots_hint >= 0 ? (slots_hint < N ? slots_hint : N) : (long long)N * k;
-  w.tc = tc && H % kTcTileM == 0 && I % kTcTileM == 0;
-  w.nt = slots_hint >= 0 ? decode_nt_routed((int)S_real, 1, E) : decode_nt_routed(N, k, E);
-  w.tn = tc_pass_tokens(S_real, E);
+  w.cb8 = cb8;
+  if (cb8) {
+    w.nt = cb8_nt_routed(S_real, E);
+    w.nt_dn = 2 * w.nt;
+  } else {
+    w.nt = slots_hint >= 0 ? decode_nt_routed((int)S_real, 1, E) : decode_nt_routed(N, k, E);
+    w.nt_dn = w.nt;
+  }
   w.nt_s = decode_nt(N);
-  const int pt = w.tc ? w.tn : 8 * w.nt;
+  const int pt = cb8 ? 4 * w.nt : 8 * w.nt;
   w.L = host_plan_layout(N, k, E, 1, pt);
   w.Rp = (int)(w.L.off[8] - w.L.off[7]);
   w.P = (int)(w.L.off[11] - w.L.off[10]);
   w.Ps = (N + 8 * w.nt_s - 1) / (8 * w.nt_s);   // shared-expert passes
   w.RB_gu = I / kRowsPerBlock;
   w.RB_dn = H / kRowsPerBlock;
-  if (w.tc) {
-    w.tail_gu = tc_tail_items((long long)w.P * (I / kTcTileM));
-    w.tail_dn = tc_tail_items((long long)w.P * (H / kTcTileM));
-    w.n_zero_routed = 2 + 4 * (w.tail_gu + w.tail_dn);
-  } else {
-    w.tail_gu = decode_tail_items((long long)w.P * w.RB_gu);
-    w.tail_dn = decode_tail_items((long long)w.P * w.RB_dn);
-    w.n_zero_routed = 2 + w.P * (w.RB_gu + w.RB_dn);
-  }
+  w.tail_gu = decode_tail_items((long long)w.P * w.RB_gu);
+  w.tail_dn = decode_tail_items((long long)w.P * w.RB_dn);
+  w.n_zero_routed = 2 + w.P * (w.RB_gu + w.RB_dn);
   w.tail_sgu = decode_tail_items((long long)w.Ps * w.RB_gu);
   w.tail_sdn = decode_tail_items((long long)w.Ps * w.RB_dn);
   w.n_zero_shared = 2 + w.Ps * (w.RB_gu + w.RB_dn);
+  const size_t h_bf16 = (size_t)w.Rp * 2 * I * 2, h_h8 = (size_t)w.Rp * (I / kStageK) * kH8StageBytes;
   w.plan = 0;
-  w.xs = align_up((size_t)w.L.off[13] * 4);
-  w.h = w.xs + (w.tc ? align_up((size_t)w.Rp * H * 2) : 0);
-  w.y = w.h + align_up((size_t)w.Rp * 2 * I * 2);
+  w.x8 = align_up((size_t)w.L.off[13] * 4);
+  w.x8s = w.x8 + align_up((size_t)N * H * 2);
+  w.h = w.x8s + align_up((size_t)N * 4);
+  w.y = w.h + align_up(h_bf16 > h_h8 ? h_bf16 : h_h8);
   w.hs = w.y + align_up((size_t)w.Rp * H * 4);
   w.ys = w.hs + align_up((size_t)N * 2 * I * 2);
   w.done = w.ys + align_up((size_t)N * H * 4);
   w.part_gu = w.done + align_up((size_t)(w.n_zero_routed + w.n_zero_shared) * 4);
-  w.part_dn = w.part_gu + align_up(w.tc ? tc_part_bytes(w.tail_gu, w.tn, 2) : decode_part_bytes(w.tail_gu, w.nt, 2));
-  w.part_sgu = w.part_dn + align_up(w.tc ? tc_part_bytes(w.tail_dn, w.tn, 1) : decode_part_bytes(w.tail_dn, w.nt, 1));
+  w.part_dn = w.part_gu + align_up(decode_part_bytes(w.tail_gu, w.nt, 2));
+  w.part_sgu = w.part_dn + align_up(decode_part_bytes(w.tail_dn, w.nt_dn, 1));
   w.part_sdn = w.part_sgu + align_up(decode_part_bytes(w.tail_sgu, w.nt_s, 2));
   w.total = w.part_sdn + align_up(decode_part_bytes(w.tail_sdn, w.nt_s, 1));
   return w;
@@ -104,19 +108,24 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 bool experts_ok(const cbmoe_experts* ex) {
   return ex && ex->E > 0 && ex->E <= 1024 && ex->H > 0 && ex->I > 0 && ex->H % kStageK == 0 &&
          ex->I % kStageK == 0 && ex->gateup_idx && ex->gateup_cb && ex->down_idx && ex->down_cb &&
-         aligned16(ex->gateup_idx) && aligned16(ex->down_idx) && aligned16(ex->gateup_cb) && aligned16(ex->down_cb);
+         aligned16(ex->gateup_idx) && aligned16(ex->down_idx) && aligned16(ex->gateup_cb) && aligned16(ex->down_cb) &&
+         (ex->gateup_cb8 == nullptr) == (ex->down_cb8 == nullptr) && aligned16(ex->gateup_cb8) &&
+         aligned16(ex->down_cb8);
+}
+
+bool has_cb8(const cbmoe_experts* ex) { return ex->gateup_cb8 != nullptr && ex->down_cb8 != nullptr; }
+
+DecodeParams base_params() {
+  DecodeParams p{};
+  p.E = 1;
+  p.sel = {0xffffffffu, 1u << 16, 1u << 29, 1u << 30, 1u << 31};
+  return p;
 }
 
 bool shared_ok(const cbmoe_shared* sh) {
   return sh && sh->gateup_q && sh->gate_s && sh->up_s && sh->down_q && sh->down_s &&
          (sh->scale_axis == 0 || sh->scale_axis == 1) && aligned16(sh->gateup_q) && aligned16(sh->down_q) &&
          aligned16(sh->gate_s) && aligned16(sh->up_s) && aligned16(sh->down_s);
-}
-
-DecodeParams base_params() {
-  DecodeParams p{};
-  p.E = 1;
-  return p;
 }
 
 // Per host thread and device: a second stream and two events, so the shared expert's gate/up (independent of
@@ -138,52 +147,71 @@ int side_stream(SideStream** out) {
   return CBMOE_OK;
 }
 
-// Plan + routed gate/up + routed down into the workspace; returns the plan pointer through *plan_out.
+// Plan + routed gate/up + routed down into the workspace (y_sorted f32, rows in plan order).
 int routed_decode(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx, const float* w, int k,
                   float limit, uint8_t* ws, const DecodeWorkspace& W, cudaStream_t stream) {
   int32_t* plan = reinterpret_cast<int32_t*>(ws + W.plan);
   int* done = reinterpret_cast<int*>(ws + W.done);
-  int rc = launch_route_plan(idx, w, N, k, ex->E, 1, W.tc ? W.tn : 8 * W.nt, plan, stream, done, W.n_zero_routed);
-  if (rc) return rc;
-  uint16_t* h = reinterpret_cast<uint16_t*>(ws + W.h);
   float* ys = reinterpret_cast<float*>(ws + W.y);
-  if (W.tc) {
-    uint16_t* xs = reinterpret_cast<uint16_t*>(ws + W.xs);
-    rc = launch_gather_perm(x, ex->H, plan + W.L.off[7], W.Rp, xs, stream);
+  if (W.cb8 && !has_cb8(ex)) return CBMOE_ERR_INVALID;   // workspace sized for tables the call does not have
+  if (W.cb8) {
+    uint8_t* x8 = ws + W.x8;
+    float* x8s = reinterpret_cast<float*>(ws + W.x8s);
+    uint8_t* h8 = ws + W.h;
+    SplitX sx;
+    sx.x = x;
+    sx.N = N;
+    sx.K = ex->H;
+    sx.x8 = x8;
+    sx.scale = x8s;
+    int rc = launch_route_plan(idx, w, N, k, ex->E, 1, 4 * W.nt, plan, stream, done, W.n_zero_routed, &sx);
     if (rc) return rc;
-    TcParams t{};
-    t.wq = static_cast<const uint8_t*>(ex->gateup_idx);
-    t.cb = static_cast<const uint32_t*>(ex->gateup_cb);
-    t.rows = ex->I;
-    t.K = ex->H;
-    t.pass_expert = plan + W.L.off[10];
-    t.pass_row0 = plan + W.L.off[11];
-    t.pass_cnt = plan + W.L.off[12];
-    t.n_pass = plan + W.L.off[5];
-    t.E = ex->E;
-    t.limit = limit;
-    t.h_out = h;
-    t.h_plane = (size_t)W.Rp * ex->I;
-    t.sched = done;
-    t.done = done + 2;
-    t.part = reinterpret_cast<float*>(ws + W.part_gu);
-    t.tail_items = W.tail_gu;
-    rc = tc_cb3_gateup(t, xs, W.Rp, W.tn, stream);
+    DecodeParams p = base_params();
+    p.wq = static_cast<const uint8_t*>(ex->gateup_idx);
+    p.cb8 = static_cast<const uint8_t*>(ex->gateup_cb8);
+    p.rows = ex->I;
+    p.K = ex->H;
+    p.RB = ex->I / kRowsPerBlock;
+    p.KS = ex->H / kStageK;
+    p.b8 = x8;
+    p.b8_scale = x8s;
+    p.tok_row = plan + W.L.off[7];
+    p.pass_expert = plan + W.L.off[10];
+    p.pass_row0 = plan + W.L.off[11];
+    p.pass_cnt = plan + W.L.off[12];
+    p.n_pass = plan + W.L.off[5];
+    p.N = N;
+    p.E = ex->E;
+    p.limit = limit;
+    p.h8_out = h8;
+    p.sched = done;
+    p.tail_items = W.tail_gu;
+    p.done = done + 2;
+    p.part = reinterpret_cast<float*>(ws + W.part_gu);
+    rc = decode_cb8_gateup(p, W.nt, stream);
     if (rc) return rc;
-    TcParams d = t;
+    DecodeParams d = p;
     d.wq = static_cast<const uint8_t*>(ex->down_idx);
-    d.cb = static_cast<const uint32_t*>(ex->down_cb);
+    d.cb8 = static_cast<const uint8_t*>(ex->down_cb8);
     d.rows = ex->H;
     d.K = ex->I;
-    d.h_out = nullptr;
+    d.RB = ex->H / kRowsPerBlock;
+    d.KS = ex->I / kStageK;
+    d.b8 = h8;
+    d.b8_scale = nullptr;
+    d.tok_row = nullptr;
+    d.h8_out = nullptr;
     d.y_out = ys;
     d.sched = done + 1;
-    d.done = done + 2 + 4 * W.tail_gu;
-    d.part = reinterpret_cast<float*>(ws + W.part_dn);
     d.tail_items = W.tail_dn;
-    return tc_cb3_down(d, h, h + t.h_plane, W.Rp, W.tn, stream);
+    d.done = done + 2 + W.P * W.RB_gu;
+    d.part = reinterpret_cast<float*>(ws + W.part_dn);
+    return decode_cb8_down(d, W.nt_dn, stream);
   }
 
+  int rc = launch_route_plan(idx, w, N, k, ex->E, 1, 8 * W.nt, plan, stream, done, W.n_zero_routed);
+  if (rc) return rc;
+  uint16_t* h = reinterpret_cast<uint16_t*>(ws + W.h);
   DecodeParams p = base_params();
   p.wq = static_cast<const uint8_t*>(ex->gateup_idx);
   p.cb = static_cast<const uint32_t*>(ex->gateup_cb);
@@ -428,20 +456,18 @@ extern "C" int cbmoe_device_errors(int clear, int* out_host) {
 
 extern "C" size_t cbmoe_workspace_bytes(const cbmoe_experts* ex, int N, int k, int path) {
   if (!ex || N < 0 || k <= 0 || ex->E <= 0) return 0;
+  if (path != CBMOE_PATH_AUTO && path != CBMOE_PATH_DECODE && path != CBMOE_PATH_GROUPED) return 0;
   if (pick_path(N, k, path) == CBMOE_PATH_GROUPED) return grouped_workspace(ex->E, ex->H, ex->I, N, k).total;
-  return decode_workspace(ex->E, ex->H, ex->I, N, k, -1, path == CBMOE_PATH_DECODE_TC).total;
+  return decode_workspace(ex->E, ex->H, ex->I, N, k, -1, has_cb8(ex)).total;
 }
 
 static int check_common(const cbmoe_experts* ex, const uint16_t* x, int N, const int32_t* idx, const float* w,
                         int k, int path) {
   if (!experts_ok(ex) || N < 0 || k <= 0 || k > 64) return CBMOE_ERR_INVALID;
   if (N > 0 && (!x || !idx || !w || !aligned16(x))) return CBMOE_ERR_INVALID;
-  if (path != CBMOE_PATH_AUTO && path != CBMOE_PATH_DECODE && path != CBMOE_PATH_GROUPED &&
-      path != CBMOE_PATH_DECODE_TC)
-    return CBMOE_ERR_INVALID;
+  if (path != CBMOE_PATH_AUTO && path != CBMOE_PATH_DECODE && path != CBMOE_PATH_GROUPED) return CBMOE_ERR_INVALID;
   if (pick_path(N, k, path) == CBMOE_PATH_GROUPED && (ex->I % kGrpTileM || ex->H % kGrpTileM || N > (1 << 24)))
     return CBMOE_ERR_UNSUPPORTED;
-  if (path == CBMOE_PATH_DECODE_TC && (ex->I % kTcTileM || ex->H % kTcTileM)) return CBMOE_ERR_UNSUPPORTED;
   return CBMOE_OK;
 }
 
@@ -462,7 +488,7 @@ extern "C" int cbmoe_experts_apply(const cbmoe_experts* ex, const uint16_t* x, i
     return launch_combine_bf16(reinterpret_cast<const uint16_t*>(ws + G.y), plan + G.L.off[9], w, N, k, ex->H,
                                nullptr, y, nullptr, stream);
   }
-  const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k, -1, path == CBMOE_PATH_DECODE_TC);
+  const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k, -1, has_cb8(ex));
   if (!workspace || workspace_bytes < W.total) return CBMOE_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   rc = routed_decode(ex, x, N, idx, w, k, limit, ws, W, stream);
@@ -513,7 +539,7 @@ extern "C" int cbmoe_moe_layer(const cbmoe_experts* ex, const cbmoe_shared* sh, 
     return launch_combine_bf16(reinterpret_cast<const uint16_t*>(ws + G.y), plan + G.L.off[9], w, N, k, ex->H, sy,
                                nullptr, out, stream);
   }
-  const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k, -1, path == CBMOE_PATH_DECODE_TC);
+  const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k, -1, has_cb8(ex));
   if (!workspace || workspace_bytes < W.total) return CBMOE_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   SideStream* side = nullptr;
@@ -549,6 +575,36 @@ extern "C" int cbmoe_cb3_matvec(const void* idx_k, const void* cb_k, int rows, i
   p.N = N;
   p.y_out = y;
   return decode_cb3_single(p, decode_nt(N), stream);
+}
+
+extern "C" size_t cbmoe_cb8_matvec_workspace_bytes(int N, int K) {
+  if (N < 0 || K <= 0 || K % kStageK) return 0;
+  return align_up((size_t)N * K * 2) + align_up((size_t)N * 4);
+}
+
+extern "C" int cbmoe_cb8_matvec(const void* idx_k, const void* cb8, int rows, int K, const uint16_t* x, int N,
+                                float* y, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!idx_k || !cb8 || rows <= 0 || K <= 0 || rows % kRowsPerBlock || K % kStageK || N < 0) return CBMOE_ERR_INVALID;
+  if (N > 0 && (!x || !y || !aligned16(x) || !aligned16(idx_k) || !aligned16(cb8))) return CBMOE_ERR_INVALID;
+  if (N == 0) return CBMOE_OK;
+  if (!workspace || workspace_bytes < cbmoe_cb8_matvec_workspace_bytes(N, K) || !aligned16(workspace))
+    return CBMOE_ERR_WORKSPACE;
+  uint8_t* x8 = static_cast<uint8_t*>(workspace);
+  float* xs = reinterpret_cast<float*>(x8 + align_up((size_t)N * K * 2));
+  int rc = launch_split_x(x, N, K, x8, xs, stream);
+  if (rc) return rc;
+  DecodeParams p = base_params();
+  p.wq = static_cast<const uint8_t*>(idx_k);
+  p.cb8 = static_cast<const uint8_t*>(cb8);
+  p.rows = rows;
+  p.K = K;
+  p.RB = rows / kRowsPerBlock;
+  p.KS = K / kStageK;
+  p.b8 = x8;
+  p.b8_scale = xs;
+  p.N = N;
+  p.y_out = y;
+  return decode_cb8_single(p, N <= 4 ? 1 : 2, stream);
 }
 
 extern "C" int cbmoe_w8_linear(const void* qk, const float* s, int scale_axis, int rows, int K, const uint16_t* x,
@@ -617,7 +673,7 @@ extern "C" int cbmoe_experts_apply_noalloc(const cbmoe_experts* ex, const uint16
   if (rc) return rc;
   if (N > 0 && (!y || !aligned16(y))) return CBMOE_ERR_INVALID;
   if (N == 0) return CBMOE_OK;
-  const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k);
+  const DecodeWorkspace W = decode_workspace(ex->E, ex->H, ex->I, N, k, -1, has_cb8(ex));
   if (W.total > kNoAllocScratchBytes) return CBMOE_ERR_WORKSPACE;   // request needs more than the fixed array
   int dev = 0;
   CBMOE_CUDA_TRY(cudaGetDevice(&dev));

@@ -2,6 +2,7 @@
 // byte permutes and the bf16 tensor-core MMA used by the decode kernels.
 #pragma once
 #include <cstdint>
+#include <mutex>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
@@ -103,22 +104,33 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   return d;
 }
 
+// The MMA wrappers below are plain (not volatile) asm: pure functions of their register operands, so the compiler
+// may schedule the next chunk's loads and table lookups around them. Shared-memory loads are ordinary C++ loads,
+// which stay after the mbarrier waits (asm with a "memory" clobber) that make the data visible.
+
 // D += A(16x16 bf16, row) * B(16x8 bf16, col), f32 accumulate.
 __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint4 lds128(const void* p) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(smem_addr(p)));
-  return v;
+// D += A(16x32 int8, row) * B(32x8 int8, col), exact int32 accumulation: A signed (s8) or unsigned (u8), B s8.
+template <bool kAUnsigned>
+__device__ __forceinline__ void mma_i8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (kAUnsigned)
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+
+// 16-byte shared-memory load (p 16-byte aligned).
+__device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -148,4 +160,29 @@ __device__ __forceinline__ float swiglu_clamped(float g, float u, float limit) {
 namespace cbmoe {
 void set_last_cuda_error(cudaError_t e);
 int num_sms();
+
+// One-time set-up per device (a kernel's shared-memory attribute, its resident grid): `init(value)` runs once for
+// each device, with that device current, under a lock; on success (CBMOE_OK) the value it set is kept for that
+// device. Kernel attributes are per device, so a process that drives several GPUs sets them on each.
+struct PerDevice {
+  std::mutex mu;
+  long long val[64] = {};
+  bool done[64] = {};
+};
+template <typename F>
+int per_device(PerDevice& pd, F&& init, long long* out) {
+  int dev = 0;
+  CBMOE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return CBMOE_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lk(pd.mu);
+  if (!pd.done[dev]) {
+    long long v = 0;
+    const int rc = init(v);
+    if (rc) return rc;
+    pd.val[dev] = v;
+    pd.done[dev] = true;
+  }
+  *out = pd.val[dev];
+  return CBMOE_OK;
+}
 }  // namespace cbmoe

@@ -16,14 +16,34 @@
 
 namespace cbmoe {
 
+// CB8 kernels come in two builds of the selector arithmetic: kFmtCB8 (part of it as multiply-adds on the FMA pipe,
+// CBMOE_CB8_FMA_MODE of cb8_dequant_chunk) and kFmtCB8A (shifts and masks on the ALU pipe).
+#ifndef CBMOE_CB8_FMA_MODE
+#define CBMOE_CB8_FMA_MODE 2
+#endif
+constexpr int kFmtCB8A = 3;
+template <>
+struct Fmt<kFmtCB8A> {
+  static constexpr int kUnitBytes = kCb3kUnitBytes;
+};
+template <int FMT>
+constexpr bool is_cb8() { return FMT == kFmtCB8 || FMT == kFmtCB8A; }
+
 template <int FMT, int NMAT, int NT, int HILO, int NSTAGE>
 struct DecodeSmem {
+  static constexpr bool kCb8 = is_cb8<FMT>();
   static constexpr int kUnit = Fmt<FMT>::kUnitBytes;
   static constexpr int kWBytes = kConsumerWarps * NMAT * kUnit;
-  static constexpr int kAuxBytes = NMAT * 1024;                // codebooks (CB3K) or scales (W8K) of the item
-  static constexpr int kBCopy = kStageK * 2 * (HILO ? 2 : 1);  // bytes of one token row per stage
+  // codebooks (CB3K), tables + row factors (CB8) or scales (W8K) of the item
+  static constexpr int kAuxBytes = NMAT * (kCb8 ? kCb8BlockBytes : 1024);
+  // bytes of one B row per stage: bf16 (x, or h as hi + lo), X8 or H8
+  static constexpr int kBCopy = kCb8 ? (HILO ? kH8StageBytes : kX8StageBytes) : kStageK * 2 * (HILO ? 2 : 1);
   static constexpr int kBRow = kBCopy + 16;                    // padded: conflict-free fragment loads
-  static constexpr int kBBytes = NT * 8 * kBRow;
+  // B rows of a pass: 8 tokens per column tile (bf16); CB8: 4 tokens (X8, hi and lo columns) or 2 slots (H8, 4
+  // part columns) per tile
+  static constexpr int kTokPerTile = kCb8 ? (HILO ? 2 : 4) : 8;
+  static constexpr int kPassTokens = NT * kTokPerTile;
+  static constexpr int kBBytes = kPassTokens * kBRow;
   static constexpr int kStage = kWBytes + kAuxBytes + kBBytes;
   static constexpr int kBarBytes = ((16 + 32) * NSTAGE + 127) / 128 * 128;   // barriers + stage headers
   static constexpr int kTotal = kBarBytes + NSTAGE * kStage;
@@ -94,6 +114,7 @@ __device__ __forceinline__ Schedule make_schedule(const DecodeParams& p, int n_i
 template <int FMT, int NMAT>
 __device__ __forceinline__ int aux_bytes(const DecodeParams& p, bool first) {
   if constexpr (FMT == kFmtCB3) return first ? NMAT * 1024 : 0;
+  else if constexpr (is_cb8<FMT>()) return first ? NMAT * kCb8BlockBytes : 0;
   else return p.scale_axis == 1 ? (first ? NMAT * kRowsPerBlock * 4 : 0) : NMAT * kStageK * 4;
 }
 
@@ -115,13 +136,23 @@ __device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, %0;" 
 #ifndef CBMOE_DECODE_MINB_NT1
 #define CBMOE_DECODE_MINB_NT1 1
 #endif
-template <int NT>
-constexpr int decode_min_blocks() { return NT == 1 ? CBMOE_DECODE_MINB_NT1 : 1; }
+// Resident CTAs the CB8 kernels are compiled for: 4 per SM for the smallest tiles (1 token tile with X8 rows, 2
+// slot tiles with H8 rows: 96 registers, no spills), 3 above.
+#ifndef CBMOE_CB8_MINB_SMALL
+#define CBMOE_CB8_MINB_SMALL 4
+#endif
+template <int FMT, int NT, int HILO>
+constexpr int decode_min_blocks() {
+  if constexpr (is_cb8<FMT>()) return (NT == (HILO ? 2 : 1)) ? CBMOE_CB8_MINB_SMALL : 3;
+  return NT == 1 ? CBMOE_DECODE_MINB_NT1 : 1;
+}
 
 template <int FMT, int NMAT, int NT, int EPI, int HILO, int NSTAGE>
-__global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<NT>()) decode_kernel_t(const DecodeParams p) {
+__global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<FMT, NT, HILO>())
+    decode_kernel_t(const DecodeParams p) {
   using SM = DecodeSmem<FMT, NMAT, NT, HILO, NSTAGE>;
-  constexpr int kPassTokens = NT * 8;
+  constexpr bool kCb8 = SM::kCb8;
+  constexpr int kPassTokens = SM::kPassTokens;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + NSTAGE;
@@ -225,6 +256,8 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<NT>()) decod
           if (aux > 0 && lane < NMAT) {
             if constexpr (FMT == kFmtCB3) {
               if (lane == 0) bulk_g2s(sa, p.cb + cb_offset_words(pi.e, rb, 0, 0, 0, RB, NMAT), aux, &full[st]);
+            } else if constexpr (kCb8) {
+              if (lane == 0) bulk_g2s(sa, p.cb8 + cb8_block_offset(pi.e, rb, RB, NMAT), aux, &full[st]);
             } else {
               const float* scl = (lane == 0) ? p.s0 : p.s1;
               const int per = aux / NMAT;
@@ -233,8 +266,11 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<NT>()) decod
             }
           }
           if (brow >= 0) {
-            const uint16_t* src =
-                p.b + (size_t)brow * (p.K * (HILO ? 2 : 1)) + (size_t)ks * kStageK * (HILO ? 2 : 1);
+            const void* src;
+            if constexpr (kCb8)
+              src = p.b8 + ((size_t)brow * KS + ks) * SM::kBCopy;
+            else
+              src = p.b + (size_t)brow * (p.K * (HILO ? 2 : 1)) + (size_t)ks * kStageK * (HILO ? 2 : 1);
             bulk_g2s(sw + SM::kWBytes + SM::kAuxBytes + lane * SM::kBRow, src, SM::kBCopy, &full[st]);
           }
           if (++st == NSTAGE) {
@@ -265,33 +301,117 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<NT>()) decod
   int st = 0;
   uint32_t ph = 0;
   Codebook cbg[NMAT], cbh[NMAT];
-  float sg[NMAT], sh[NMAT];
+  Cb8 c8g[NMAT], c8h[NMAT];
+  float sg[NMAT], sh[NMAT];   // W8K row scales; CB8 row factors
   // Few accumulator tiles per warp (NT * NMAT <= 2) make a long chain of dependent MMAs per stage; a second set
-  // (odd MMA steps, or the h-lo products with HILO) halves it and is added in before the epilogue.
-  constexpr int kAccSets = (NT * NMAT <= 2) ? 2 : 1;
+  // (odd MMA steps, the h-lo products with HILO, or the lo-part products of CB8) halves it and is added in before
+  // the epilogue. (CB8 accumulates in int32: over the item with X8 rows, per chunk with H8 rows.)
+  constexpr int kAccSets = (NT * NMAT <= 2 && !kCb8) ? 2 : 1;
+  // Token (or slot) of a column of this lane's accumulator tile n, register i: bf16 tiles hold 8 tokens (columns
+  // 2t, 2t+1 = two tokens); CB8 X8 tiles 4 tokens (columns 2t, 2t+1 = hi and lo of token t); CB8 H8 tiles 2 slots
+  // (columns 2t, 2t+1 = two of the 4 parts of slot t/2). Partial sums are kept per column, j = n*8 + 2t + (i&1).
+  auto col_tok = [&](int n, int i) -> int {
+    if constexpr (!kCb8) return n * 8 + 2 * t + (i & 1);
+    else if constexpr (HILO) return n * 2 + (t >> 1);
+    else return n * 4 + t;
+  };
+  __shared__ float s_hmax[kConsumerWarps][8];   // CB8 SwiGLU epilogue: per-warp |h| maxima of each token
   float acc[NMAT][NT][4];
   float acc_b[kAccSets > 1 ? NMAT : 1][NT][4];
+  // CB8 with X8 rows: exact int32 sums of the hi-byte and lo-byte products over the item (converted to acc, as
+  // 256 hi + lo, when the segment ends)
+  int ci_hi[kCb8 && !HILO ? NMAT : 1][NT][4], ci_lo[kCb8 && !HILO ? NMAT : 1][NT][4];
 
   // Epilogue of one item from acc (the item's full sums).
   auto epilogue = [&](const StageHdr& e) {
     const int rowbase = e.rb * kRowsPerBlock + warp * kRowsPerWarp;
+    if constexpr (kCb8) {
+      if constexpr (EPI == kEpiStore && HILO) {
+        // down (H8 rows): the 4 part columns of a slot are spread over lane pairs (t, t^1)
 #pragma unroll
-    for (int n = 0; n < NT; ++n) {
+        for (int n = 0; n < NT; ++n) {
+          float vg = acc[0][n][0] + acc[0][n][1], vh = acc[0][n][2] + acc[0][n][3];
+          vg += __shfl_xor_sync(0xffffffffu, vg, 1);
+          vh += __shfl_xor_sync(0xffffffffu, vh, 1);
+          const int j = col_tok(n, 0);
+          if ((t & 1) || j >= e.cnt) continue;
+          float* y = p.y_out + (size_t)(e.row0 + j) * p.rows + rowbase + g;
+          y[0] = vg;
+          y[8] = vh;
+        }
+      } else {
+        // X8 rows: token t's low-digit column and high-digit column (x 256), times the token's factor (the sums
+        // already carry the row factors)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int j = n * 8 + 2 * t + (i & 1);
-        const int r = rowbase + g + ((i & 2) ? 8 : 0);
-        if (j >= e.cnt) continue;
-        const int row = e.row0 + j;
-        if constexpr (EPI == kEpiSwiglu) {
-          const float hv = swiglu_clamped(acc[0][n][i], acc[NMAT - 1][n][i], p.limit);
-          const __nv_bfloat16 hi = __float2bfloat16_rn(hv);
-          const __nv_bfloat16 lo = __float2bfloat16_rn(hv - __bfloat162float(hi));
-          uint16_t* dst = p.h_out + (size_t)row * (2 * p.rows) + (r / kStageK) * (2 * kStageK) + (r % kStageK);
-          dst[0] = *reinterpret_cast<const uint16_t*>(&hi);
-          dst[kStageK] = *reinterpret_cast<const uint16_t*>(&lo);
-        } else {
-          p.y_out[(size_t)row * p.rows + r] = acc[0][n][i];
+        for (int n = 0; n < NT; ++n) {
+          const int j = col_tok(n, 0);
+          float fx = 0.f;
+          if (j < e.cnt) fx = p.b8_scale[p.tok_row ? p.tok_row[e.row0 + j] : e.row0 + j];
+          const float g0 = (acc[0][n][0] + acc[0][n][1] * 256.f) * fx;
+          const float h0 = (acc[0][n][2] + acc[0][n][3] * 256.f) * fx;
+          if constexpr (EPI == kEpiStore) {
+            if (j < e.cnt) {
+              float* y = p.y_out + (size_t)(e.row0 + j) * p.rows + rowbase + g;
+              y[0] = g0;
+              y[8] = h0;
+            }
+          } else {
+            // SwiGLU, then h as 4 signed base-256 digits with one factor per (token, 64-row block): the block's
+            // largest |h| times 2^u in [2^28, 2^29)
+            const float g1 = (acc[NMAT - 1][n][0] + acc[NMAT - 1][n][1] * 256.f) * fx;
+            const float h1 = (acc[NMAT - 1][n][2] + acc[NMAT - 1][n][3] * 256.f) * fx;
+            float hg = 0.f, hh = 0.f;
+            if (j < e.cnt) {
+              hg = swiglu_clamped(g0, g1, p.limit);
+              hh = swiglu_clamped(h0, h1, p.limit);
+            }
+            float mx = fmaxf(fabsf(hg), fabsf(hh));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            consumer_bar();   // the previous item's readers are done with s_hmax
+            if (g == 0) s_hmax[warp][n * 4 + t] = mx;
+            consumer_bar();
+            mx = fmaxf(fmaxf(s_hmax[0][n * 4 + t], s_hmax[1][n * 4 + t]),
+                       fmaxf(s_hmax[2][n * 4 + t], s_hmax[3][n * 4 + t]));
+            if (j >= e.cnt) continue;
+            const int u = shift_for(mx, 29);
+            const int ksd = p.rows / kStageK;
+            uint8_t* stage8 = p.h8_out + ((size_t)(e.row0 + j) * ksd + (e.rb >> 2)) * kH8StageBytes;
+            uint8_t* row8 = stage8 + (e.rb & 3) * 256 + warp * kRowsPerWarp + g;
+            int vg = __float2int_rn(ldexpf(hg, u)), vh = __float2int_rn(ldexpf(hh, u));
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int dg = (q < 3) ? (int)(int8_t)(vg & 0xff) : vg;   // balanced digits; the last one takes the rest
+              const int dh = (q < 3) ? (int)(int8_t)(vh & 0xff) : vh;
+              row8[q * 64] = (uint8_t)dg;
+              row8[q * 64 + 8] = (uint8_t)dh;
+              vg = (vg - dg) >> 8;
+              vh = (vh - dh) >> 8;
+            }
+            if (warp == 0 && g == 0) *reinterpret_cast<float*>(stage8 + 1024 + (e.rb & 3) * 4) = ldexpf(1.f, -u);
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int j = n * 8 + 2 * t + (i & 1);
+          const int r = rowbase + g + ((i & 2) ? 8 : 0);
+          if (j >= e.cnt) continue;
+          const int row = e.row0 + j;
+          if constexpr (EPI == kEpiSwiglu) {
+            const float hv = swiglu_clamped(acc[0][n][i], acc[NMAT - 1][n][i], p.limit);
+            const __nv_bfloat16 hi = __float2bfloat16_rn(hv);
+            const __nv_bfloat16 lo = __float2bfloat16_rn(hv - __bfloat162float(hi));
+            uint16_t* dst = p.h_out + (size_t)row * (2 * p.rows) + (r / kStageK) * (2 * kStageK) + (r % kStageK);
+            dst[0] = *reinterpret_cast<const uint16_t*>(&hi);
+            dst[kStageK] = *reinterpret_cast<const uint16_t*>(&lo);
+          } else {
+            p.y_out[(size_t)row * p.rows + r] = acc[0][n][i];
+          }
         }
       }
     }
@@ -300,7 +420,7 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<NT>()) decod
   // its arrival on the item's counter (fence + atomic) is counted after the next stage, and the atomic's result is
   // read when the next piece or item ends (or when the consumers stop), so no global round trip stalls the MMAs.
   // The last arriver adds the Q slots up and runs the epilogue.
-  constexpr int kSlotFloats = kPassTokens * NMAT * kRowsPerBlock;
+  constexpr int kSlotFloats = NT * 8 * NMAT * kRowsPerBlock;   // columns x matrices x rows
   int pend_state = 0;   // 0: nothing pending, 1: partials stored, 2: arrival counted (ticket in thread 0)
   StageHdr pend{};
   int ticket = 0;
@@ -333,7 +453,7 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<NT>()) decod
           const int j = n * 8 + 2 * t + (i & 1);
           const int rl = rl0 + ((i & 2) ? 8 : 0);
           float v = 0.f;
-          if (j < pend.cnt)
+          if (col_tok(n, i) < pend.cnt)
             for (int q = 0; q < nseg; ++q) v += __ldcg(&p.part[slot_at(pend.item, q, j, m, rl)]);
           acc[m][n][i] = v;
         }
@@ -361,6 +481,14 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<NT>()) decod
           cbg[m] = {ca.x, ca.y, ca.z, ca.w};
           cbh[m] = {cb.x, cb.y, cb.z, cb.w};
           sg[m] = sh[m] = 0.f;
+        } else if constexpr (kCb8) {
+          const uint4 ca = lds128(sa + ((warp * NMAT + m) * 16 + g) * 16);
+          const uint4 cb = lds128(sa + ((warp * NMAT + m) * 16 + g + 8) * 16);
+          c8g[m] = {ca.x, ca.y, ca.z, ca.w};
+          c8h[m] = {cb.x, cb.y, cb.z, cb.w};
+          const float* rf = reinterpret_cast<const float*>(sa + NMAT * 1024) + (warp * NMAT + m) * 16;
+          sg[m] = rf[g];
+          sh[m] = rf[g + 8];
         } else {
           const float* sc = reinterpret_cast<const float*>(sa) + m * kRowsPerBlock + warp * kRowsPerWarp;
           sg[m] = (p.scale_axis == 1) ? sc[g] : 0.f;
@@ -373,12 +501,13 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<NT>()) decod
           for (int i = 0; i < 4; ++i) {
             acc[m][n][i] = 0.f;
             if constexpr (kAccSets > 1) acc_b[m][n][i] = 0.f;
+            if constexpr (kCb8 && !HILO) ci_hi[m][n][i] = ci_lo[m][n][i] = 0;
           }
       }
     }
 
     uint32_t wd[NMAT][12];
-    if constexpr (FMT == kFmtCB3) {
+    if constexpr (FMT == kFmtCB3 || kCb8) {
 #pragma unroll
       for (int m = 0; m < NMAT; ++m) {
         const uint8_t* u = sw + (warp * NMAT + m) * SM::kUnit + lane * 48;
@@ -393,6 +522,51 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<NT>()) decod
       }
     }
 
+    if constexpr (kCb8) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        // B fragments: column g of tile n = token n*4 + g/2, part g%2 (X8) or slot n*2 + g/4, part g%4 (H8);
+        // one 16-byte load gives both k32 steps (x, y: step 0; z, w: step 1)
+        uint4 bx[NT];
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          if (n == 0 || n * SM::kTokPerTile < h.cnt) {
+            const int brow = n * SM::kTokPerTile + (HILO ? (g >> 2) : (g >> 1));
+            const int part = HILO ? (g & 3) : (g & 1);
+            bx[n] = lds128(sb + brow * SM::kBRow + c * (HILO ? 256 : 128) + part * 64 + 16 * t);
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+          uint32_t ah[2][4], al[2][4];
+          cb8_dequant_chunk<FMT == kFmtCB8 ? CBMOE_CB8_FMA_MODE : 0>(wd[m][3 * c], wd[m][3 * c + 1],
+                                                                      wd[m][3 * c + 2], c8g[m], c8h[m], p.sel, ah, al);
+#pragma unroll
+          for (int n = 0; n < NT; ++n) {
+            if (!(n == 0 || n * SM::kTokPerTile < h.cnt)) continue;
+            if constexpr (HILO) {
+              // this chunk's exact products (T = 256 hi + lo), then times the factor of the chunk and of the part
+              // (digit p of the slot's h: 256^p)
+              int dh[4] = {0, 0, 0, 0}, dl[4] = {0, 0, 0, 0};
+              mma_i8<false>(dh, ah[0], bx[n].x, bx[n].y);
+              mma_i8<true>(dl, al[0], bx[n].x, bx[n].y);
+              mma_i8<false>(dh, ah[1], bx[n].z, bx[n].w);
+              mma_i8<true>(dl, al[1], bx[n].z, bx[n].w);
+              const float F = *reinterpret_cast<const float*>(sb + (n * 2 + (t >> 1)) * SM::kBRow + 1024 + 4 * c);
+              const float f0 = (t & 1) ? F * 65536.f : F, f1 = f0 * 256.f;
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                acc[m][n][i] += (float)(dh[i] * 256 + dl[i]) * ((i & 1) ? f1 : f0);
+            } else {
+              mma_i8<false>(ci_hi[m][n], ah[0], bx[n].x, bx[n].y);
+              mma_i8<true>(ci_lo[m][n], al[0], bx[n].x, bx[n].y);
+              mma_i8<false>(ci_hi[m][n], ah[1], bx[n].z, bx[n].w);
+              mma_i8<true>(ci_lo[m][n], al[1], bx[n].z, bx[n].w);
+            }
+          }
+        }
+      }
+    } else {
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       uint32_t bf[NT][8];
@@ -445,6 +619,7 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<NT>()) decod
         }
       }
     }
+    }   // bf16 formats
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
     if (++st == NSTAGE) {
@@ -455,6 +630,19 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<NT>()) decod
     if (!(h.flags & 2)) continue;
 
     // ---------------------------------------------------------------------------------- item epilogue
+    // CB8: the segment's sums times the row factors now, while they are the item's: a cut item's epilogue runs
+    // later (in its last-arriving piece), after this warp may have loaded the next item's.
+    if constexpr (kCb8) {
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float v = (HILO ? acc[m][n][i] : (float)ci_hi[m][n][i] * 256.f + (float)ci_lo[m][n][i]);
+            acc[m][n][i] = v * ((i & 2) ? sh[m] : sg[m]);
+          }
+    }
     if constexpr (kAccSets > 1) {
 #pragma unroll
       for (int m = 0; m < NMAT; ++m)
@@ -472,7 +660,7 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<NT>()) decod
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int j = n * 8 + 2 * t + (i & 1);
-            if (j < h.cnt) p.part[slot_at(h.item, h.kq, j, m, rl0 + ((i & 2) ? 8 : 0))] = acc[m][n][i];
+            if (col_tok(n, i) < h.cnt) p.part[slot_at(h.item, h.kq, j, m, rl0 + ((i & 2) ? 8 : 0))] = acc[m][n][i];
           }
       if (pend_state == 2) resolve();   // the previous segment's; acc is free again
       pend = h;
@@ -540,14 +728,17 @@ template <int FMT, int NMAT, int NT, int EPI, int HILO, int NSTAGE>
 int launch_decode_t(const DecodeParams& p, int kind, cudaStream_t stream) {
   using SM = DecodeSmem<FMT, NMAT, NT, HILO, NSTAGE>;
   auto kern = decode_kernel_t<FMT, NMAT, NT, EPI, HILO, NSTAGE>;
-  static int grid = 0;
-  if (grid == 0) {
+  static PerDevice s_grid;
+  long long grid = 0;
+  int rc = per_device(s_grid, [&](long long& v) -> int {
     CBMOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kTotal));
     int per_sm = 0;
     CBMOE_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecodeThreads, SM::kTotal));
-    grid = num_sms() * (per_sm > 0 ? per_sm : 1);
-  }
-  const int g = (p.grid_cap > 0 && p.grid_cap < grid) ? p.grid_cap : grid;
+    v = (long long)num_sms() * (per_sm > 0 ? per_sm : 1);
+    return CBMOE_OK;
+  }, &grid);
+  if (rc) return rc;
+  const int g = (p.grid_cap > 0 && p.grid_cap < grid) ? p.grid_cap : (int)grid;
   prof_begin(kind, stream);
   kern<<<g, kDecodeThreads, SM::kTotal, stream>>>(p);
   prof_end(kind, stream);
@@ -583,6 +774,70 @@ int launch_combine(const float* y_sorted, const int* row_slot, const float* wts,
   prof_begin(kProfCombine, stream);
   combine_kernel<<<blocks, 256, 0, stream>>>(y_sorted, row_slot, wts, N, topk, H, add, out_f32, out_bf16);
   prof_end(kProfCombine, stream);
+  CBMOE_CUDA_TRY(cudaGetLastError());
+  return CBMOE_OK;
+}
+
+// Ring stages of the CB8 kernels: 3 with X8 rows (a gate+up stage is 17-19 KB), 4 with H8 rows (down: 12-16 KB),
+// so that the resident CTAs fit the SM's shared memory.
+#ifndef CBMOE_STAGES_CB8_X8
+#define CBMOE_STAGES_CB8_X8 3
+#endif
+#ifndef CBMOE_STAGES_CB8_H8
+#define CBMOE_STAGES_CB8_H8 4
+#endif
+#ifndef CBMOE_CB8_SEL_FMA
+#define CBMOE_CB8_SEL_FMA 0
+#endif
+// Selector arithmetic of the CB8 kernels: on the ALU pipe (default: shorter dependency latency, measured faster)
+// or on the FMA pipe (CBMOE_CB8_SEL=fma in the environment, read once: a measurement switch).
+static int cb8_fmt() {
+  static int f = -1;
+  if (f < 0) {
+    const char* e = getenv("CBMOE_CB8_SEL");
+    f = (e && e[0] == 'f') ? kFmtCB8 : (e && e[0] == 'a') ? kFmtCB8A : (CBMOE_CB8_SEL_FMA ? kFmtCB8 : kFmtCB8A);
+  }
+  return f;
+}
+
+template <int FMT, int NMAT, int EPI, int HILO>
+int launch_cb8_nt(const DecodeParams& p, int nt, int kind, cudaStream_t stream) {
+  constexpr int NS = HILO ? CBMOE_STAGES_CB8_H8 : CBMOE_STAGES_CB8_X8;
+  if constexpr (HILO != 0) {   // slot tiles of 2: 2 or 4 tiles (passes of up to 4 or 8 slots)
+    if (nt <= 2) return launch_decode_t<FMT, NMAT, 2, EPI, HILO, NS>(p, kind, stream);
+    return launch_decode_t<FMT, NMAT, 4, EPI, HILO, NS>(p, kind, stream);
+  } else {
+    if (nt <= 1) return launch_decode_t<FMT, NMAT, 1, EPI, HILO, NS>(p, kind, stream);
+    return launch_decode_t<FMT, NMAT, 2, EPI, HILO, NS>(p, kind, stream);
+  }
+}
+
+int decode_cb8_gateup(const DecodeParams& p, int nt, cudaStream_t s) {
+  return cb8_fmt() == kFmtCB8 ? launch_cb8_nt<kFmtCB8, 2, kEpiSwiglu, 0>(p, nt, kProfCb3GateUp, s)
+                              : launch_cb8_nt<kFmtCB8A, 2, kEpiSwiglu, 0>(p, nt, kProfCb3GateUp, s);
+}
+int decode_cb8_down(const DecodeParams& p, int nt, cudaStream_t s) {
+  return cb8_fmt() == kFmtCB8 ? launch_cb8_nt<kFmtCB8, 1, kEpiStore, 1>(p, nt, kProfCb3Down, s)
+                              : launch_cb8_nt<kFmtCB8A, 1, kEpiStore, 1>(p, nt, kProfCb3Down, s);
+}
+int decode_cb8_single(const DecodeParams& p, int nt, cudaStream_t s) {
+  return cb8_fmt() == kFmtCB8 ? launch_cb8_nt<kFmtCB8, 1, kEpiStore, 0>(p, nt, kProfCb3Single, s)
+                              : launch_cb8_nt<kFmtCB8A, 1, kEpiStore, 0>(p, nt, kProfCb3Single, s);
+}
+
+__global__ void split_x_kernel(const uint16_t* __restrict__ x, int N, int K, uint8_t* __restrict__ x8,
+                               float* __restrict__ scale) {
+  __shared__ float red[32];
+  for (int r = blockIdx.x; r < N; r += gridDim.x)
+    split_x_row(x + (size_t)r * K, K, x8 + (size_t)r * (K / kStageK) * kX8StageBytes, scale + r, red);
+}
+
+int launch_split_x(const uint16_t* x, int N, int K, uint8_t* x8, float* scale, cudaStream_t stream) {
+  if (N <= 0) return CBMOE_OK;
+  const int blocks = N < num_sms() * 4 ? N : num_sms() * 4;
+  prof_begin(kProfOther, stream);
+  split_x_kernel<<<blocks, 256, 0, stream>>>(x, N, K, x8, scale);
+  prof_end(kProfOther, stream);
   CBMOE_CUDA_TRY(cudaGetLastError());
   return CBMOE_OK;
 }

@@ -96,7 +96,7 @@ struct EpWorkspace {
   lyr::GroupedWorkspace Gr;    // received rows, grouped path
 };
 
-EpWorkspace ep_workspace(int E_loc, int H, int I, int N_local, int k, int nranks, int cap, int path) {
+EpWorkspace ep_workspace(int E_loc, int H, int I, int N_local, int k, int nranks, int cap, int path, int cb8) {
   using lyr::align_up;
   EpWorkspace w;
   w.R = nranks * cap;
@@ -109,7 +109,7 @@ EpWorkspace ep_workspace(int E_loc, int H, int I, int N_local, int k, int nranks
   w.y_recv = w.ones + align_up((size_t)w.R * 4);
   w.y_back = w.y_recv + align_up((size_t)w.R * H * 4);
   w.sub_local = w.y_back + align_up((size_t)w.R * H * 4);
-  w.Wl = lyr::decode_workspace(E_loc, H, I, N_local, k);
+  w.Wl = lyr::decode_workspace(E_loc, H, I, N_local, k, -1, 0);   // shared-expert regions only
   w.sub_recv = w.sub_local + align_up(w.Wl.total);
   // The receive buffer holds up to R rows, but a rank expects about its own slot count (N_local * k) of real
   // ones: AUTO chooses the kernels by that. From 8 rows per local expert on, the tensor-core GEMMs, except where
@@ -131,7 +131,7 @@ EpWorkspace ep_workspace(int E_loc, int H, int I, int N_local, int k, int nranks
     w.Gr = lyr::grouped_workspace(E_loc, H, I, w.R, 1);
     rb = w.Gr.total;
   } else {
-    w.Wr = lyr::decode_workspace(E_loc, H, I, w.R, 1, expect);
+    w.Wr = lyr::decode_workspace(E_loc, H, I, w.R, 1, expect, cb8);
     rb = w.Wr.total;
   }
   w.total = w.sub_recv + align_up(rb);
@@ -200,7 +200,7 @@ extern "C" size_t cbmoe_ep_workspace_bytes(const cbmoe_experts* local, int N_loc
                                            int path) {
   if (!local || local->E <= 0 || N_local < 0 || k <= 0 || nranks < 1 || capacity <= 0) return 0;
   if (path != CBMOE_PATH_AUTO && path != CBMOE_PATH_DECODE && path != CBMOE_PATH_GROUPED) return 0;
-  return ep_workspace(local->E, local->H, local->I, N_local, k, nranks, capacity, path).total;
+  return ep_workspace(local->E, local->H, local->I, N_local, k, nranks, capacity, path, lyr::has_cb8(local)).total;
 }
 
 extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_experts* local, int E_total,
@@ -216,7 +216,8 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
   const int E_loc = local->E, H = local->H, I = local->I;
   EpPeer* pe = static_cast<EpPeer*>(peer_v);
   if (pe && !ep_peer_matches(pe, nranks, rank, H, capacity)) return CBMOE_ERR_INVALID;
-  const EpWorkspace W = ep_workspace(E_loc, H, I, N_local, k, nranks, capacity, path);
+  if (ep_peer_poisoned(pe)) return CBMOE_ERR_DEVICE;   // a wait of an earlier call gave up
+  const EpWorkspace W = ep_workspace(E_loc, H, I, N_local, k, nranks, capacity, path, lyr::has_cb8(local));
   if (!workspace || workspace_bytes < W.total) return CBMOE_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint16_t* send_x = reinterpret_cast<uint16_t*>(ws + W.send_x);

@@ -38,6 +38,11 @@ struct EpPeer {
   uint8_t* own = nullptr;
   PeerPtrs peers{};
   uint32_t seq = 0;
+  // Poison word in mapped pinned host memory: a wait kernel that gave up sets it; from then on the transport's
+  // kernels write nothing to peers and wait for nothing, and cbmoe_ep_layer returns CBMOE_ERR_DEVICE (it reads
+  // the host side without synchronizing) until the peer is destroyed and set up again.
+  volatile int* poison_host = nullptr;
+  int* poison_dev = nullptr;
 };
 
 namespace {
@@ -67,11 +72,16 @@ __device__ __forceinline__ void signal_peers(uint32_t* ctr, const PeerPtrs& peer
   }
 }
 
+__device__ __forceinline__ bool poisoned(const int* poison) {
+  return *reinterpret_cast<const volatile int*>(poison) != 0;
+}
+
 // Token rows of the kept slots -> in_x[rank][pos] of their destination; all (peer, row) ids -> in_meta[rank][..].
 __global__ void ep_dispatch_kernel(const uint4* __restrict__ x, int H16, const int32_t* __restrict__ slot_pos,
                                    int S, int k, const int32_t* __restrict__ send_meta, int nranks, int rank,
                                    int cap, PeerPtrs peers, size_t off_x, size_t off_meta, size_t off_flag,
-                                   uint32_t* ctr, uint32_t seq) {
+                                   uint32_t* ctr, uint32_t seq, const int* poison) {
+  if (poisoned(poison)) return;   // an earlier wait gave up: the peers' buffers are no longer in step
   const long long rows_work = (long long)S * H16;
   const long long total = rows_work + (long long)nranks * cap;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -97,7 +107,9 @@ __global__ void ep_dispatch_kernel(const uint4* __restrict__ x, int H16, const i
 template <typename T>
 __global__ void ep_return_kernel(const T* __restrict__ y_sorted, const int32_t* __restrict__ row_slot,
                                  const int32_t* __restrict__ recv_meta, int R, int H, int cap, int nranks, int rank,
-                                 PeerPtrs peers, size_t off_y, size_t off_flag, uint32_t* ctr, uint32_t seq) {
+                                 PeerPtrs peers, size_t off_y, size_t off_flag, uint32_t* ctr, uint32_t seq,
+                                 const int* poison) {
+  if (poisoned(poison)) return;
   const int H16 = H * (int)sizeof(T) / 16;
   const size_t row_stride = (size_t)H * sizeof(T);   // packed [nranks][cap][H] rows of T
   const long long total = (long long)R * H16;
@@ -114,16 +126,20 @@ __global__ void ep_return_kernel(const T* __restrict__ y_sorted, const int32_t* 
   signal_peers(ctr, peers, nranks, rank, off_flag, seq);
 }
 
-// One CTA: wait until every source's flag reached seq (bounded; CBMOE_DEVERR_TIMEOUT and return on expiry).
-__global__ void ep_wait_kernel(const uint32_t* flags, int nranks, uint32_t seq) {
+// One CTA: wait until every source's flag reached seq (bounded; on expiry CBMOE_DEVERR_TIMEOUT, the poison word
+// is set and the kernel returns). A poisoned transport waits for nothing.
+__global__ void ep_wait_kernel(const uint32_t* flags, int nranks, uint32_t seq, int* poison) {
   const int t = threadIdx.x;
-  if (t < nranks) {
+  if (t < nranks && !poisoned(poison)) {
     const unsigned long long t0 = globaltimer_ns();
     while ((int)(ld_acquire_sys(flags + t) - seq) < 0) {
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
         atomicOr(&g_device_errors, CBMOE_DEVERR_TIMEOUT);
+        *reinterpret_cast<volatile int*>(poison) = 1;
+        __threadfence_system();
         break;
       }
+      if (poisoned(poison)) break;   // another waiter of this call gave up
       __nanosleep(64);
     }
   }
@@ -148,8 +164,9 @@ int ep_peer_dispatch(EpPeer* pe, const uint16_t* x, int H, const int32_t* slot_p
   prof_begin(kProfExchange, stream);
   ep_dispatch_kernel<<<grid_for((long long)S * H16 + (long long)pe->nranks * pe->cap), 256, 0, stream>>>(
       reinterpret_cast<const uint4*>(x), H16, slot_pos, S, k, send_meta, pe->nranks, pe->rank, pe->cap, pe->peers,
-      pe->off_x, pe->off_meta, pe->off_fx, ctr, pe->seq);
-  ep_wait_kernel<<<1, 64, 0, stream>>>(reinterpret_cast<const uint32_t*>(pe->own + pe->off_fx), pe->nranks, pe->seq);
+      pe->off_x, pe->off_meta, pe->off_fx, ctr, pe->seq, pe->poison_dev);
+  ep_wait_kernel<<<1, 64, 0, stream>>>(reinterpret_cast<const uint32_t*>(pe->own + pe->off_fx), pe->nranks, pe->seq,
+                                       pe->poison_dev);
   prof_end(kProfExchange, stream);
   prof_add_launches(2);
   CBMOE_CUDA_TRY(cudaGetLastError());
@@ -164,12 +181,13 @@ int ep_peer_return(EpPeer* pe, const void* y_sorted, bool bf16, const int32_t* r
   if (bf16)
     ep_return_kernel<uint16_t><<<grid_for(work), 256, 0, stream>>>(
         static_cast<const uint16_t*>(y_sorted), row_slot, recv_meta, R, H, pe->cap, pe->nranks, pe->rank, pe->peers,
-        pe->off_y, pe->off_fy, ctr, pe->seq);
+        pe->off_y, pe->off_fy, ctr, pe->seq, pe->poison_dev);
   else
     ep_return_kernel<float><<<grid_for(work), 256, 0, stream>>>(
         static_cast<const float*>(y_sorted), row_slot, recv_meta, R, H, pe->cap, pe->nranks, pe->rank, pe->peers,
-        pe->off_y, pe->off_fy, ctr, pe->seq);
-  ep_wait_kernel<<<1, 64, 0, stream>>>(reinterpret_cast<const uint32_t*>(pe->own + pe->off_fy), pe->nranks, pe->seq);
+        pe->off_y, pe->off_fy, ctr, pe->seq, pe->poison_dev);
+  ep_wait_kernel<<<1, 64, 0, stream>>>(reinterpret_cast<const uint32_t*>(pe->own + pe->off_fy), pe->nranks, pe->seq,
+                                       pe->poison_dev);
   prof_end(kProfExchange, stream);
   prof_add_launches(2);
   CBMOE_CUDA_TRY(cudaGetLastError());
@@ -182,10 +200,19 @@ void* ep_peer_in_y(EpPeer* pe) { return pe->own + pe->off_y; }
 bool ep_peer_matches(const EpPeer* pe, int nranks, int rank, int H, int cap) {
   return pe && pe->nranks == nranks && pe->rank == rank && pe->H == H && cap == pe->cap;
 }
+bool ep_peer_poisoned(const EpPeer* pe) { return pe && pe->poison_host && *pe->poison_host != 0; }
 
 }  // namespace cbmoe
 
 using namespace cbmoe;
+
+// What every rank contributes to the set-up all-gather: its (H, capacity, nranks) and its buffer's IPC handle.
+// Every rank sees every record, so every rank reaches the same verdict on a mismatch.
+struct PeerRecord {
+  int32_t H, cap, nranks, magic;
+  cudaIpcMemHandle_t handle;
+};
+constexpr int32_t kPeerMagic = 0x63626d65;   // "cbme"
 
 extern "C" int cbmoe_ep_peer_init(void* comm_v, int nranks, int rank, int H, int capacity, cudaStream_t stream,
                                   void** peer_out) {
@@ -208,38 +235,57 @@ extern "C" int cbmoe_ep_peer_init(void* comm_v, int nranks, int rank, int H, int
   pe->off_ctr = pe->off_fy + 256;
   pe->bytes = pe->off_ctr + 256;
   int rc = CBMOE_OK;
-  uint8_t* handles_dev = nullptr;
-  std::vector<uint8_t> handles((size_t)nranks * sizeof(cudaIpcMemHandle_t));
-  cudaIpcMemHandle_t mine;
+  uint8_t* records_dev = nullptr;
+  std::vector<PeerRecord> records(nranks);
+  PeerRecord mine{};
+  mine.H = H;
+  mine.cap = capacity;
+  mine.nranks = nranks;
+  mine.magic = kPeerMagic;
+  void* poison = nullptr;
   if (cudaMalloc(&pe->own, pe->bytes) != cudaSuccess || cudaMemset(pe->own, 0, pe->bytes) != cudaSuccess ||
-      cudaIpcGetMemHandle(&mine, pe->own) != cudaSuccess ||
-      cudaMalloc(&handles_dev, handles.size()) != cudaSuccess ||
-      cudaMemcpy(handles_dev + (size_t)rank * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice) !=
+      cudaIpcGetMemHandle(&mine.handle, pe->own) != cudaSuccess ||
+      cudaHostAlloc(&poison, sizeof(int), cudaHostAllocMapped) != cudaSuccess ||
+      cudaMalloc(&records_dev, records.size() * sizeof(PeerRecord)) != cudaSuccess ||
+      cudaMemcpy(records_dev + (size_t)rank * sizeof(PeerRecord), &mine, sizeof(mine), cudaMemcpyHostToDevice) !=
           cudaSuccess) {
     rc = CBMOE_ERR_CUDA;
   }
-  if (!rc && ncclAllGather(handles_dev + (size_t)rank * sizeof(mine), handles_dev, sizeof(mine), ncclUint8, comm,
-                           stream) != ncclSuccess)
-    rc = CBMOE_ERR_NCCL;
-  if (!rc && (cudaStreamSynchronize(stream) != cudaSuccess ||
-              cudaMemcpy(handles.data(), handles_dev, handles.size(), cudaMemcpyDeviceToHost) != cudaSuccess))
-    rc = CBMOE_ERR_CUDA;
+  if (poison) {
+    pe->poison_host = static_cast<volatile int*>(poison);
+    *pe->poison_host = 0;
+    if (!rc && cudaHostGetDevicePointer(reinterpret_cast<void**>(&pe->poison_dev), poison, 0) != cudaSuccess)
+      rc = CBMOE_ERR_CUDA;
+  }
+  // Every rank takes part in the all-gather even when its own set-up failed (the others would wait for it); a
+  // failed rank contributes a zeroed record, which the others reject as a mismatch.
+  if (records_dev && ncclAllGather(records_dev + (size_t)rank * sizeof(PeerRecord), records_dev,
+                                   sizeof(PeerRecord), ncclUint8, comm, stream) != ncclSuccess)
+    rc = rc ? rc : CBMOE_ERR_NCCL;
+  if (records_dev && (cudaStreamSynchronize(stream) != cudaSuccess ||
+                      cudaMemcpy(records.data(), records_dev, records.size() * sizeof(PeerRecord),
+                                 cudaMemcpyDeviceToHost) != cudaSuccess))
+    rc = rc ? rc : CBMOE_ERR_CUDA;
+  // Equal (H, capacity) on every rank: a sender computes its peers' row addresses from its own capacity.
+  for (int d = 0; d < nranks && !rc; ++d)
+    if (records[d].magic != kPeerMagic || records[d].H != H || records[d].cap != capacity ||
+        records[d].nranks != nranks)
+      rc = CBMOE_ERR_INVALID;
   for (int d = 0; d < nranks && !rc; ++d) {
     if (d == rank) {
       pe->peers.base[d] = pe->own;
       continue;
     }
-    cudaIpcMemHandle_t h;
-    memcpy(&h, handles.data() + (size_t)d * sizeof(h), sizeof(h));
     void* p = nullptr;
-    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) rc = CBMOE_ERR_CUDA;
+    if (cudaIpcOpenMemHandle(&p, records[d].handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) rc = CBMOE_ERR_CUDA;
     pe->peers.base[d] = static_cast<uint8_t*>(p);
   }
-  if (handles_dev) cudaFree(handles_dev);
+  if (records_dev) cudaFree(records_dev);
   if (rc) {
     for (int d = 0; d < nranks; ++d)
       if (d != rank && pe->peers.base[d]) cudaIpcCloseMemHandle(pe->peers.base[d]);
     if (pe->own) cudaFree(pe->own);
+    if (poison) cudaFreeHost(poison);
     delete pe;
     return rc;
   }
@@ -255,6 +301,7 @@ extern "C" int cbmoe_ep_peer_destroy(void* peer_v) {
     if (d != pe->rank && pe->peers.base[d] && cudaIpcCloseMemHandle(pe->peers.base[d]) != cudaSuccess)
       rc = CBMOE_ERR_CUDA;
   if (pe->own && cudaFree(pe->own) != cudaSuccess) rc = CBMOE_ERR_CUDA;
+  if (pe->poison_host && cudaFreeHost(const_cast<int*>(pe->poison_host)) != cudaSuccess) rc = CBMOE_ERR_CUDA;
   delete pe;
   return rc;
 }

@@ -428,11 +428,14 @@ int launch_grouped(const GroupedParams& p, const void* b, int b_rows, int kind, 
   int rc = make_token_map(&map, b, p.K, b_rows, TN);
   if (rc) return rc;
   auto kern = grouped_kernel<FMT, NMAT, EPI, TN>;
-  static bool attr = false;
-  if (!attr) {
+  static PerDevice s_attr;
+  long long set = 0;
+  rc = per_device(s_attr, [&](long long& v) -> int {
     CBMOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
-    attr = true;
-  }
+    v = 1;
+    return CBMOE_OK;
+  }, &set);
+  if (rc) return rc;
   prof_begin(kind, stream);
   kern<<<num_sms(), kGrpThreads, C::kSmem, stream>>>(p, map);
   prof_end(kind, stream);

@@ -3,7 +3,6 @@
 #pragma once
 #include "decode.cuh"
 #include "grouped.cuh"
-#include "tcdecode.cuh"
 
 namespace cbmoe {
 namespace lyr {
@@ -14,10 +13,10 @@ struct PlanLayoutHost {
 
 // Workspace of the decode path (layout documented at decode_workspace in capi.cu).
 struct DecodeWorkspace {
-  size_t plan, xs, h, y, hs, ys, done, part_gu, part_dn, part_sgu, part_sdn, total;
-  int tc;                                     // routed experts on the tcgen05 decode kernels (tcdecode.cu)
-  int tn;                                     // their token rows per pass
-  int nt, nt_s, Rp, P, Ps, RB_gu, RB_dn;
+  size_t plan, x8, x8s, h, y, hs, ys, done, part_gu, part_dn, part_sgu, part_sdn, total;
+  int cb8;                                    // routed experts on the CB8 (int8-digit) kernels
+  int nt, nt_dn;                              // column tiles of the routed gate/up and down kernels
+  int nt_s, Rp, P, Ps, RB_gu, RB_dn;
   int tail_gu, tail_dn, tail_sgu, tail_sdn;   // partial-sum space of each launch, in tail items
   int n_zero_routed, n_zero_shared;           // arrival counters (words)
   PlanLayoutHost L;
@@ -60,12 +59,13 @@ PlanLayoutHost host_plan_layout(int T, int k, int E, int tm, int pass_tokens);
 int decode_nt(int N);
 int decode_nt_routed(int N, int k, int E);
 // slots_hint: the slots expected to be real when N*k counts empty ones too (< 0: N*k); picks the token tile.
-// tc: routed experts on the tcgen05 decode kernels (CBMOE_PATH_DECODE_TC) instead of the mma.sync ones.
-DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k, long long slots_hint = -1, int tc = 0);
+// cb8: the experts carry CB8 tables (cbmoe_experts.gateup_cb8 / down_cb8), so the CB8 kernels run.
+DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k, long long slots_hint, int cb8);
 GroupedWorkspace grouped_workspace(int E, int H, int I, int N, int k);
 int pick_path(int N, int k, int path);
 bool aligned16(const void* p);
 bool experts_ok(const cbmoe_experts* ex);
+bool has_cb8(const cbmoe_experts* ex);
 bool shared_ok(const cbmoe_shared* sh);
 DecodeParams base_params();
 int side_stream(SideStream** out);
@@ -79,6 +79,7 @@ int routed_grouped(const cbmoe_experts* ex, const uint16_t* x, int N, const int3
 // Peer-memory transport of the expert-parallel layer (ep_peer.cu).
 struct EpPeer;
 bool ep_peer_matches(const EpPeer* pe, int nranks, int rank, int H, int cap);
+bool ep_peer_poisoned(const EpPeer* pe);
 int ep_peer_dispatch(EpPeer* pe, const uint16_t* x, int H, const int32_t* slot_pos, int S, int k,
                      const int32_t* send_meta, cudaStream_t stream);
 int ep_peer_return(EpPeer* pe, const void* y_sorted, bool bf16, const int32_t* row_slot, const int32_t* recv_meta,

@@ -22,6 +22,24 @@
 //
 // W8K unit (4096 B): int8, ordered [chunk c][row half h][lane][16 B]: lane (g, t)'s 16 inputs [16t, 16t+16) of
 // row g (h = 0) or g+8 (h = 1); lanes contiguous so a warp's 16-byte shared loads are conflict-free.
+//
+// CB8 (the decode kernels' codebooks, built at load time from the CB3K ones): every row's 8 bf16 entries as 16-bit
+// fixed point, T = rint(v 2^s) with the row's largest magnitude times 2^s in [2^14, 2^15), stored as two byte
+// tables: hi = T >> 8 (int8) and lo = T & 255 (uint8), so T = 256 hi + lo, plus the row factor 2^-s. T equals
+// v 2^s exactly for every entry within 2^7 of the row's largest (bf16 has 8 significant bits); smaller entries are
+// rounded to within 2^-15 of the largest. The same CB3K index bits select the bytes: one `prmt` looks up 4
+// weights' hi bytes, one their lo bytes, and each feeds an int8 m16n8k32 MMA (exact int32 sums).
+// Per (expert, 64-row block): tables [w][m][row 0..15] x 16 B (hi bytes of entries 0-3 | 4-7, lo bytes of 0-3 |
+// 4-7), then row factors 2^-s [w][m][row 0..15] x f32.
+// The m16n8k32 fragment: a lane's A register 0 / 2 hold row g's physical inputs 16t+8h+{0..3} / {4..7} of MMA step
+// h (0, 1) of a chunk, registers 1 / 3 row g+8's; B register 0 / 1 hold the same inputs of one column: the CB3K
+// selector groups s = 2h, 2h+1 unchanged, and a column's 8 inputs of step h are 8 consecutive bytes.
+// Activations reach these kernels split into signed digits the same way: "X8" rows (split_x_row) hold, per
+// 256-input stage, [chunk 4][digit 2][64] int8 with one factor f per row: x = f (256 d1 + d0), the row's largest
+// |x| / f in [2^13, 2^14) (exact for bf16 within 2^6 of the row's largest, else to within 2^-14 of it); "H8" rows
+// (the SwiGLU epilogue of the CB8 gate/up kernel) hold [chunk 4][digit 4][64] int8 then 4 f32 factors (one per
+// 64-input chunk): h = f_c sum_p 256^p d_p, the chunk's largest |h| / f_c in [2^28, 2^29) (the fp32 value itself
+// for every element within 2^5 of the chunk's largest).
 #pragma once
 #include <cstdint>
 #include "common.cuh"
@@ -37,6 +55,11 @@ constexpr int kCb3kUnitBytes = 32 * 48;                       // 1536
 constexpr int kW8kUnitBytes = 4 * 2 * 32 * 16;                // 4096
 constexpr int kFmtCB3 = 0;
 constexpr int kFmtW8 = 1;
+constexpr int kFmtCB8 = 2;
+constexpr int kCb8RowBytes = 16 + 4;                           // tables + row factor
+constexpr int kCb8BlockBytes = kRowsPerBlock * kCb8RowBytes;   // per matrix and 64-row block: 1280
+constexpr int kX8StageBytes = 4 * 2 * 64;                      // 512
+constexpr int kH8StageBytes = 4 * 4 * 64 + 16;                 // 1040: parts + 4 chunk factors
 
 template <int FMT>
 struct Fmt;
@@ -48,10 +71,105 @@ template <>
 struct Fmt<kFmtW8> {
   static constexpr int kUnitBytes = kW8kUnitBytes;
 };
+template <>
+struct Fmt<kFmtCB8> {
+  static constexpr int kUnitBytes = kCb3kUnitBytes;   // the CB3K index bits
+};
 
 struct Codebook {
   uint32_t la, lb, ha, hb;
 };
+
+// CB8 tables of one row: hi bytes (int8) of entries 0-3 | 4-7, lo bytes (uint8) of 0-3 | 4-7.
+struct Cb8 {
+  uint32_t ha, hb, la, lb;
+};
+
+// Operands the selector arithmetic takes from the kernel parameters, so that it compiles to integer multiply-adds
+// (FMA pipe) rather than shifts and masks (ALU pipe, which the table lookups keep busy): -1, 2^16, 2^29, 2^30, 2^31.
+struct SelConst {
+  uint32_t m1, s16, s29, s30, s31;
+};
+
+__device__ __forceinline__ uint32_t mul_hi(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t mad_hi(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("mad.hi.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t mad_lo(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// One chunk of one CB8 matrix: the 3 CB3K index words of this lane -> int8 A fragments of the hi and lo bytes for
+// the chunk's two k32 MMA steps: ah[h] / al[h] = {row g group 2h, row g+8 group 2h, row g group 2h+1, row g+8
+// group 2h+1}. Selectors as cb3k_dequant_chunk; the spare-bit word and the upper halves come from multiply-adds:
+// w - (w & 0x77777777) = the spare bits, mul.hi by 2^(32-n) = a right shift by n.
+// kSel: 0 = every selector operation on the ALU pipe; 1 = the spare-bit word and the upper halves on the FMA pipe
+// (multiply-adds); 2 = only the upper halves (4 independent multiply-highs) on the FMA pipe.
+template <int kSel>
+__device__ __forceinline__ void cb8_dequant_chunk(uint32_t w0, uint32_t w1, uint32_t w2, const Cb8& cg,
+                                                  const Cb8& ch, const SelConst& k, uint32_t (&ah)[2][4],
+                                                  uint32_t (&al)[2][4]) {
+  const uint32_t g01 = w0 & 0x77777777u;
+  const uint32_t g23 = w1 & 0x77777777u;
+  const uint32_t h01 = w2 & 0x77777777u;
+  uint32_t h23, g01u, g23u, h01u, h23u;
+  if constexpr (kSel == 1) {
+    const uint32_t s0 = mad_lo(g01, k.m1, w0), s1 = mad_lo(g23, k.m1, w1), s2 = mad_lo(h01, k.m1, w2);
+    h23 = mad_hi(s0, k.s29, mad_hi(s1, k.s30, mul_hi(s2, k.s31)));
+    g01u = mul_hi(g01, k.s16);
+    g23u = mul_hi(g23, k.s16);
+    h01u = mul_hi(h01, k.s16);
+    h23u = mul_hi(h23, k.s16);
+  } else if constexpr (kSel == 2) {
+    h23 = ((w0 >> 3) & 0x11111111u) | ((w1 >> 2) & 0x22222222u) | ((w2 >> 1) & 0x44444444u);
+    g01u = mul_hi(g01, k.s16);
+    g23u = mul_hi(g23, k.s16);
+    h01u = mul_hi(h01, k.s16);
+    h23u = mul_hi(h23, k.s16);
+  } else {
+    h23 = ((w0 >> 3) & 0x11111111u) | ((w1 >> 2) & 0x22222222u) | ((w2 >> 1) & 0x44444444u);
+    g01u = g01 >> 16;
+    g23u = g23 >> 16;
+    h01u = h01 >> 16;
+    h23u = h23 >> 16;
+  }
+  ah[0][0] = prmt(cg.ha, cg.hb, g01);
+  ah[0][1] = prmt(ch.ha, ch.hb, h01);
+  ah[0][2] = prmt(cg.ha, cg.hb, g01u);
+  ah[0][3] = prmt(ch.ha, ch.hb, h01u);
+  ah[1][0] = prmt(cg.ha, cg.hb, g23);
+  ah[1][1] = prmt(ch.ha, ch.hb, h23);
+  ah[1][2] = prmt(cg.ha, cg.hb, g23u);
+  ah[1][3] = prmt(ch.ha, ch.hb, h23u);
+  al[0][0] = prmt(cg.la, cg.lb, g01);
+  al[0][1] = prmt(ch.la, ch.lb, h01);
+  al[0][2] = prmt(cg.la, cg.lb, g01u);
+  al[0][3] = prmt(ch.la, ch.lb, h01u);
+  al[1][0] = prmt(cg.la, cg.lb, g23);
+  al[1][1] = prmt(ch.la, ch.lb, h23);
+  al[1][2] = prmt(cg.la, cg.lb, g23u);
+  al[1][3] = prmt(ch.la, ch.lb, h23u);
+}
+
+// The shift that brings the largest magnitude m into [2^(top-1), 2^top): top - e, where m = f 2^e, f in [0.5, 1)
+// (frexp's exponent); 0 when m is zero or not finite (nothing to scale).
+__device__ __forceinline__ int shift_for(float m, int top) {
+  if (!(m > 0.f && m < 3e38f)) return 0;
+  int ex = 0;
+  frexpf(m, &ex);
+  return top - ex;
+}
+
+// 2^k as a float (k in [-126, 127]).
+__device__ __forceinline__ float pow2f(int k) { return __int_as_float((127 + k) << 23); }
 
 // One chunk of one matrix: 3 index words of this lane -> fragments a[s][0..3] for the 4 MMA steps.
 //   selectors of row g:   w0 & 0x7.. (s = 0 low half, s = 1 high half), w1 & 0x7.. (s = 2, 3)
@@ -117,6 +235,38 @@ __device__ __forceinline__ void w8k_dequant_chunk(const uint4& qg, const uint4& 
   }
 }
 
+// X8 rows: one CTA per row. The row's largest |x| sets the factor: X = rint(x 2^t), largest |X| in [2^13, 2^14);
+// digits d1 = (X + 128) >> 8, d0 = X - 256 d1 (both int8): x = 2^-t (256 d1 + d0).
+__device__ inline void split_x_row(const uint16_t* __restrict__ xr, int K, uint8_t* __restrict__ out,
+                                   float* __restrict__ scale, float* red) {
+  float mx = 0.f;
+  for (int i = threadIdx.x; i < K; i += blockDim.x)
+    mx = fmaxf(mx, fabsf(__uint_as_float((uint32_t)xr[i] << 16)));
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, d));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
+  __syncthreads();   // red is reused by the next row
+  const int sh = shift_for(mx, 14);
+  if (threadIdx.x == 0) *scale = ldexpf(1.f, -sh);
+  for (int i = 2 * threadIdx.x; i < K; i += 2 * blockDim.x) {
+    uint32_t dig[2][2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int X = __float2int_rn(ldexpf(__uint_as_float((uint32_t)xr[i + e] << 16), sh));
+      const int d1 = (X + 128) >> 8;
+      dig[e][1] = (uint32_t)d1 & 0xffu;
+      dig[e][0] = (uint32_t)(X - 256 * d1) & 0xffu;
+    }
+    const int ks = i / kStageK, c = (i % kStageK) / kChunkK, q = i % kChunkK;
+    uint8_t* o = out + (size_t)ks * kX8StageBytes + c * 128 + q;
+    *reinterpret_cast<uint16_t*>(o) = (uint16_t)(dig[0][0] | (dig[1][0] << 8));
+    *reinterpret_cast<uint16_t*>(o + 64) = (uint16_t)(dig[0][1] | (dig[1][1] << 8));
+  }
+}
+
 __host__ __device__ inline size_t unit_offset(int e, int rb, int ks, int w, int m, int RB, int KS, int nmat,
                                               int unit_bytes) {
   return (((((size_t)e * RB + rb) * KS + ks) * kWarpsPerBlock + w) * nmat + m) * (size_t)unit_bytes;
@@ -124,6 +274,11 @@ __host__ __device__ inline size_t unit_offset(int e, int rb, int ks, int w, int 
 
 __host__ __device__ inline size_t cb_offset_words(int e, int rb, int w, int m, int r16, int RB, int nmat) {
   return ((((size_t)e * RB + rb) * kWarpsPerBlock + w) * nmat + m) * 64 + (size_t)r16 * 4;
+}
+
+// Byte offset of the CB8 block of (expert e, 64-row block rb).
+__host__ __device__ inline size_t cb8_block_offset(int e, int rb, int RB, int nmat) {
+  return ((size_t)e * RB + rb) * nmat * kCb8BlockBytes;
 }
 
 }  // namespace cbmoe

@@ -4,7 +4,7 @@
 //   scan    per-expert totals -> padded row starts, block starts, pass starts, active list (warp scans)
 //   pass C  each warp re-walks its range; a slot's sorted row = its expert's row start + the slots of that expert
 //           in earlier warps + earlier slots in this warp: the same order as a stable argsort.
-#include "common.cuh"
+#include "decode.cuh"
 #include "profile.cuh"
 
 namespace cbmoe {
@@ -59,10 +59,21 @@ __device__ __forceinline__ int warp_exclusive_scan(int v, int* total) {
   return x - v;
 }
 
+// CTA 0 builds the plan; CTAs 1.. (when split.x8 is set) write the X8 rows of split.x, which the expert kernels
+// after the plan read (independent work sharing the launch).
 __global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(const int32_t* __restrict__ idx,
                                                                   const float* __restrict__ wts, int T, int k, int E,
                                                                   int tm, int pass_tokens, int32_t* __restrict__ plan,
-                                                                  PlanLayout L, int* __restrict__ zero, int n_zero) {
+                                                                  PlanLayout L, int* __restrict__ zero, int n_zero,
+                                                                  SplitX split) {
+  if (blockIdx.x > 0) {
+    __shared__ float s_red[32];
+    const int KS = split.K / kStageK;
+    for (int r = blockIdx.x - 1; r < split.N; r += gridDim.x - 1)
+      split_x_row(split.x + (size_t)r * split.K, split.K, split.x8 + (size_t)r * KS * kX8StageBytes, split.scale + r,
+                  s_red);
+    return;
+  }
   extern __shared__ int sm[];
   int* cnt = sm;                               // [kPlanWarps][E]
   int* counts = cnt + kPlanWarps * E;          // [E]
@@ -449,22 +460,31 @@ __global__ void __launch_bounds__(kPlanCtaWarps * 32) plan_place_kernel(const in
 size_t plan_smem_bytes(int E) { return (size_t)(kPlanWarps + 2) * E * sizeof(int); }
 
 int launch_route_plan(const int32_t* idx, const float* w, int T, int k, int E, int tm, int pass_tokens,
-                      int32_t* plan, cudaStream_t stream, int* zero, int n_zero) {
+                      int32_t* plan, cudaStream_t stream, int* zero, int n_zero, const SplitX* split) {
   const PlanLayout L = plan_layout(T, k, E, tm, pass_tokens);
   const size_t smem = plan_smem_bytes(E);
-  static bool attr_set = false;
-  if (!attr_set) {
+  static PerDevice s_attr;
+  long long set = 0;
+  const int arc = per_device(s_attr, [&](long long& v) -> int {
     CBMOE_CUDA_TRY(cudaFuncSetAttribute(route_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)plan_smem_bytes(kPlanMaxExperts)));
     CBMOE_CUDA_TRY(cudaFuncSetAttribute(plan_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         kPlanCtaWarps * kPlanMaxExperts * 4));
     CBMOE_CUDA_TRY(cudaFuncSetAttribute(plan_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         kPlanCtaWarps * kPlanMaxExperts * 4));
-    attr_set = true;
-  }
+    v = 1;
+    return CBMOE_OK;
+  }, &set);
+  if (arc) return arc;
   const long long S = (long long)T * k;
   const int n_chunks = (int)((S + kPlanChunkSlots - 1) / kPlanChunkSlots);
+  SplitX sx{};
+  if (split != nullptr && split->x8 != nullptr && split->N > 0) sx = *split;
   if (S > kPlanBigSlots && n_chunks <= kPlanMaxChunks) {
+    if (sx.x8 != nullptr) {
+      const int rc = launch_split_x(sx.x, sx.N, sx.K, sx.x8, sx.scale, stream);
+      if (rc) return rc;
+    }
     int32_t* chunk = plan + L.off[12] + ((L.off[11] - L.off[10] + 3) & ~3);   // scratch after the pass lists
     const size_t csmem = (size_t)kPlanCtaWarps * E * 4;
     prof_begin(kProfPlan, stream);
@@ -478,7 +498,10 @@ int launch_route_plan(const int32_t* idx, const float* w, int T, int k, int E, i
     return CBMOE_OK;
   }
   prof_begin(kProfPlan, stream);
-  route_plan_kernel<<<1, kPlanThreads, smem, stream>>>(idx, w, T, k, E, tm, pass_tokens, plan, L, zero, n_zero);
+  int blocks = 1;
+  if (sx.x8 != nullptr) blocks += sx.N < num_sms() * 2 ? sx.N : num_sms() * 2;
+  route_plan_kernel<<<blocks, kPlanThreads, smem, stream>>>(idx, w, T, k, E, tm, pass_tokens, plan, L, zero, n_zero,
+                                                            sx);
   prof_end(kProfPlan, stream);
   CBMOE_CUDA_TRY(cudaGetLastError());
   return CBMOE_OK;

@@ -227,6 +227,62 @@ static bool cb3k_shape_ok(int nmat, int E, int rows, int K) {
   return E > 0 && rows > 0 && K > 0 && rows % kRowsPerBlock == 0 && K % kStageK == 0 && (nmat == 1 || nmat == 2);
 }
 
+namespace cbmoe {
+namespace {
+
+// CB8 tables of one row from its CB3K codebook words (layout.cuh): T = rint(v 2^s), the largest |v| 2^s in
+// [2^14, 2^15) (at most 255 * 2^7 for bf16 entries, so T fits 16 bits); hi = T >> 8, lo = T & 255; row factor 2^-s.
+// A row of zeros (or of non-finite entries) gets s = 0.
+__global__ void cb8_build_kernel(const uint32_t* __restrict__ cbk, int nmat, int E, int rows,
+                                 uint8_t* __restrict__ out) {
+  const long long total = (long long)E * rows * nmat;
+  for (long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x; tid < total;
+       tid += (long long)gridDim.x * blockDim.x) {
+    // tid = (((e*RB + rb)*4 + w)*nmat + m)*16 + r16: the CB3K codebook order
+    const long long blk = tid / (kRowsPerBlock * nmat);   // e*RB + rb
+    const int in_blk = (int)(tid % (kRowsPerBlock * nmat));   // (w*nmat + m)*16 + r16
+    const uint32_t* wds = cbk + tid * 4;
+    float v[8];
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t lo = (wds[i >> 2] >> (8 * (i & 3))) & 0xffu;
+      const uint32_t hi = (wds[2 + (i >> 2)] >> (8 * (i & 3))) & 0xffu;
+      v[i] = __uint_as_float(((hi << 8) | lo) << 16);
+      mx = fmaxf(mx, fabsf(v[i]));
+    }
+    const int sh = shift_for(mx, 15);
+    uint32_t hw[2] = {0, 0}, lw[2] = {0, 0};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int T = __float2int_rn(ldexpf(v[i], sh));
+      hw[i >> 2] |= ((uint32_t)(T >> 8) & 0xffu) << (8 * (i & 3));
+      lw[i >> 2] |= ((uint32_t)T & 0xffu) << (8 * (i & 3));
+    }
+    uint8_t* b = out + blk * (size_t)nmat * kCb8BlockBytes;
+    *reinterpret_cast<uint4*>(b + (size_t)in_blk * 16) = make_uint4(hw[0], hw[1], lw[0], lw[1]);
+    reinterpret_cast<float*>(b + (size_t)nmat * kRowsPerBlock * 16)[in_blk] = ldexpf(1.f, -sh);
+  }
+}
+
+}  // namespace
+}  // namespace cbmoe
+
+extern "C" size_t cbmoe_cb8_bytes(int E, int rows, int nmat) {
+  if (E <= 0 || rows <= 0 || rows % cbmoe::kRowsPerBlock || nmat < 1 || nmat > 2) return 0;
+  return (size_t)E * rows * nmat * cbmoe::kCb8RowBytes;
+}
+
+extern "C" int cbmoe_cb8_build(const void* cb_k, int nmat, int E, int rows, void* cb8, cudaStream_t stream) {
+  if (!cb3k_shape_ok(nmat, E, rows, cbmoe::kStageK) || !cb_k || !cb8 || !aligned16(cb_k) || !aligned16(cb8))
+    return CBMOE_ERR_INVALID;
+  const long long n = (long long)E * rows * nmat;
+  cbmoe::cb8_build_kernel<<<grid_for(n, 256), 256, 0, stream>>>(static_cast<const uint32_t*>(cb_k), nmat, E, rows,
+                                                                  static_cast<uint8_t*>(cb8));
+  CBMOE_CUDA_TRY(cudaGetLastError());
+  return CBMOE_OK;
+}
+
 extern "C" int cbmoe_cb3k_repack(const uint32_t* idx0, const uint16_t* cb0, const uint32_t* idx1,
                                  const uint16_t* cb1, int nmat, int E, int rows, int K, void* idx_k, void* cb_k,
                                  cudaStream_t stream) {

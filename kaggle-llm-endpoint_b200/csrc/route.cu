@@ -144,10 +144,15 @@ extern "C" int cbmoe_route(const uint16_t* x, int N, int D, const uint16_t* rout
   if (!x || !router_w || !bias || !idx || !w) return CBMOE_ERR_INVALID;
   const size_t smem = (size_t)kRouteWarps * kRouteTok * E * sizeof(float) + (size_t)kRouteTok * D * sizeof(uint16_t);
   if (smem > 200 * 1024) return CBMOE_ERR_UNSUPPORTED;   // D up to ~8000 at E = 256
-  static size_t attr = 0;
-  if (smem > 48 * 1024 && smem > attr) {
-    CBMOE_CUDA_TRY(cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr = smem;
+  if (smem > 48 * 1024) {   // the largest size the kernel may be given, once per device
+    static PerDevice s_attr;
+    long long set = 0;
+    const int rc = per_device(s_attr, [&](long long& v) -> int {
+      CBMOE_CUDA_TRY(cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+      v = 1;
+      return CBMOE_OK;
+    }, &set);
+    if (rc) return rc;
   }
   const int blocks = (N + kRouteTok - 1) / kRouteTok;
   prof_begin(kProfOther, stream);

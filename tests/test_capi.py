@@ -97,6 +97,11 @@ def test_workspace_queries_without_gpu(L):
     ex = Experts(160, 5120, 1536, 16, 16, 16, 16)
     dec = [L.cbmoe_workspace_bytes(ctypes.byref(ex), n, 8, 1) for n in (1, 8, 64)]
     assert all(v > 0 for v in dec) and dec[0] <= dec[1] <= dec[2]
-    assert L.cbmoe_workspace_bytes(ctypes.byref(ex), 8, 8, 3) > dec[1]             # CBMOE_PATH_DECODE_TC
+    assert L.cbmoe_workspace_bytes(ctypes.byref(ex), 8, 8, 3) == 0                 # not a path
+    ex8 = Experts(160, 5120, 1536, 16, 16, 16, 16, 16, 16)                          # with CB8 tables
+    assert L.cbmoe_workspace_bytes(ctypes.byref(ex8), 8, 8, 1) > 0
+    assert L.cbmoe_cb8_matvec_workspace_bytes(1, 2048) >= 2048 * 2 + 4
+    assert L.cbmoe_cb8_matvec_workspace_bytes(1, 100) == 0                          # K % 256 != 0
+    assert L.cbmoe_cb8_bytes(160, 1536, 2) == 160 * 1536 * 2 * 20
     assert L.cbmoe_workspace_bytes(ctypes.byref(ex), 4096, 8, 2) > dec[2]          # grouped, config 3
     assert L.cbmoe_ep_workspace_bytes(ctypes.byref(Experts(20, 5120, 1536, 16, 16, 16, 16)), 32, 8, 8, 64, 0) > 0

@@ -11,7 +11,7 @@ import pytest
 import torch
 
 from helpers import bf16_bits_of, shared_to_gpu, t_bf16, table_to_gpu, t_u32
-from oracle import cb3, gen, moe, q8
+from oracle import cb3, gen, moe, q8, split8
 
 pytestmark = pytest.mark.gpu
 
@@ -60,6 +60,39 @@ def test_w8k_dequant_bit_exact(cbmoe, axis, nmat):
     for m in range(nmat):
         want = q8.dequant(*leaves[m]).T.view(np.uint16)          # [in, out] -> [out, in]
         assert np.array_equal(out[m], want)
+
+
+def _wide_codebooks(rng, E, rows):
+    """Codebooks with the edge cases of the CB8 split: all-zero rows, rows with tiny and huge entries beside
+    ordinary ones, entries far below their row's largest, negative-only rows, subnormal bf16 values."""
+    cb = cb3.make_codebooks(rng, (E, rows)).astype(np.float32)
+    flat = cb.reshape(-1, 8)
+    n = flat.shape[0]
+    flat[0::17] = 0.0
+    flat[1::17, 3] = 3e-7                                         # 2^-22-ish beside entries ~0.02
+    flat[2::17] *= 1e4                                            # large rows
+    flat[3::17] = -np.abs(flat[3::17])
+    flat[4::17, :4] = 1e-39                                       # bf16 subnormals
+    flat[5::17] *= 1e-30
+    flat[6::17, 0] = -2.5e-3
+    flat[7::17] = np.linspace(-0.75, 0.6, 8)                      # largest magnitude in [0.5, 1)
+    flat[8::17] = 1.0
+    return flat.reshape(E, rows, 8).astype(cb3.BF16)
+
+
+@pytest.mark.parametrize("nmat,E,rows", [(1, 2, 64), (2, 3, 128), (1, 1, 1024)])
+def test_cb8_tables_bit_exact(cbmoe, nmat, E, rows):
+    """The CB8 tables built on the GPU (int8 hi / uint8 lo bytes + row factors) equal the oracle's, byte for byte."""
+    rng = np.random.default_rng(300 + rows)
+    K = 256
+    tabs = [(cb3.pack(cb3.make_indices(rng, (E, rows, K))), _wide_codebooks(rng, E, rows)) for _ in range(nmat)]
+    g = [table_to_gpu(t) for t in tabs]
+    _, cb_k = cbmoe.ops.pack_cb3(g[0][0], g[0][1], *(g[1] if nmat == 2 else (None, None)))
+    got = cbmoe.ops.build_cb8(cb_k, nmat, E, rows).cpu().numpy()
+    want = split8.cb8_table([t[1] for t in tabs])
+    assert got.shape == want.shape
+    assert np.array_equal(got, want)
+    _no_device_errors(cbmoe)
 
 
 # ------------------------------------------------------------------------------------------------ routing plan
@@ -118,6 +151,32 @@ def test_cb3_matvec_config0_shape(cbmoe, N):
     _no_device_errors(cbmoe)
 
 
+@pytest.mark.parametrize("N", [1, 4, 5, 13, 40])
+def test_cb8_matvec_config0_shape(cbmoe, N):
+    """The int8 decode kernel on the config-0 matrix; its workspace holds the split activations, which must equal
+    the oracle's X8 rows byte for byte."""
+    c = gen.config0(seed=N)
+    rng = np.random.default_rng(N)
+    x = gen.activations(rng, N, 2048)
+    if N == 5:
+        x[1] = 0.0                                            # an all-zero token
+        x[2] *= 1e3                                           # a large one
+        x[3] = np.clip(x[3], -0.9, 0.9)                       # and one whose largest magnitude is in [0.5, 1)
+    x = x.astype(cb3.BF16)
+    idx_k, cb_k = cbmoe.ops.pack_cb3(t_u32(c["idx"][None]), t_bf16(c["cb"][None]))
+    cb8 = cbmoe.ops.build_cb8(cb_k, 1, 1, 1024)
+    ws = torch.empty(cbmoe.lib().cbmoe_cb8_matvec_workspace_bytes(N, 2048), dtype=torch.uint8, device="cuda")
+    y = cbmoe.ops.cb8_matvec(idx_k, cb8, 1024, 2048, t_bf16(x), ws=ws).cpu().numpy()
+    want = cb3.matvec(c["idx"], c["cb"], x.astype(np.float32))
+    assert moe.max_rel_err(y, want) < MATVEC_TOL
+    x8, xs = split8.split_x(x)
+    w = ws.cpu().numpy()
+    assert np.array_equal(w[:x8.size].reshape(x8.shape), x8)
+    off = -(-x8.size // 256) * 256
+    assert np.array_equal(w[off:off + 4 * N].view(np.float32), xs)
+    _no_device_errors(cbmoe)
+
+
 @pytest.mark.parametrize("axis", [0, 1])
 @pytest.mark.parametrize("N", [1, 9, 33])
 def test_w8_linear(cbmoe, axis, N):
@@ -137,49 +196,50 @@ def _layer(seed, E, H, I, axis=1):
     return rng, L
 
 
-def _pack(cbmoe, L):
+def _pack(cbmoe, L, tables="int8"):
     return cbmoe.pack_layer(table_to_gpu(L["gate"]), table_to_gpu(L["up"]), table_to_gpu(L["down"]),
-                            shared_to_gpu(L["shared"]))
+                            shared_to_gpu(L["shared"]), decode_tables=tables)
 
 
-@pytest.mark.parametrize("path", ["decode", "decode_tc"])
+@pytest.mark.parametrize("tables", ["int8", "bf16"])
 @pytest.mark.parametrize("N,k,E,zipf", [(1, 8, 16, None), (3, 4, 16, None), (8, 8, 24, None), (20, 6, 16, 1.1),
                                         (64, 8, 32, 1.1), (40, 2, 4, None)])
-def test_experts_apply_decode(cbmoe, N, k, E, zipf, path):
+def test_experts_apply_decode(cbmoe, N, k, E, zipf, tables):
     H, I = 512, 256
     rng, L = _layer(N * 31 + E, E, H, I)
     x = gen.activations(rng, N, H)
     idx, w = gen.routing(rng, N, E, k, zipf=zipf)
-    p = _pack(cbmoe, L)
-    fetch = cbmoe.ResidentFetch(path=path)
+    p = _pack(cbmoe, L, tables)
+    fetch = cbmoe.ResidentFetch(path="decode")
     y = fetch.apply(p, t_bf16(x), torch.from_numpy(idx).cuda(), torch.from_numpy(w).cuda(), 0, gen.LIMIT)
     want = moe.decode_apply(x.astype(np.float32), idx, w, L["gate"], L["up"], L["down"], gen.LIMIT)
     assert moe.max_rel_err(y.cpu().numpy(), want) < LAYER_TOL
     _no_device_errors(cbmoe)
 
 
-@pytest.mark.parametrize("path", ["decode", "decode_tc"])
+@pytest.mark.parametrize("tables", ["int8", "bf16"])
 @pytest.mark.parametrize("axis", [1, 0])
 @pytest.mark.parametrize("N", [1, 8, 24])
-def test_moe_layer_decode(cbmoe, N, axis, path):
+def test_moe_layer_decode(cbmoe, N, axis, tables):
     E, H, I, k = 16, 512, 256, 8
     rng, L = _layer(N + 7 * axis, E, H, I, axis)
     x = gen.activations(rng, N, H)
     idx, w = gen.routing(rng, N, E, k)
-    p = _pack(cbmoe, L)
+    p = _pack(cbmoe, L, tables)
     out = cbmoe.moe_dense(p, t_bf16(x), torch.from_numpy(idx).cuda(), torch.from_numpy(w).cuda(), gen.LIMIT,
-                          cbmoe.ResidentFetch(path=path))
+                          cbmoe.ResidentFetch(path="decode"))
     want = moe.moe_layer(x.astype(np.float32), idx, w, L["gate"], L["up"], L["down"], L["shared"], gen.LIMIT)
     assert out.dtype == torch.bfloat16
     assert moe.max_rel_err(out.float().cpu().numpy(), want) < LAYER_TOL
     _no_device_errors(cbmoe)
 
 
-def test_decode_composition_reference_fixture(cbmoe):
+@pytest.mark.parametrize("tables", ["int8", "bf16"])
+def test_decode_composition_reference_fixture(cbmoe, tables):
     """The reference's own `_apply_kernel` composition (executed on a NumPy stand-in) vs the CUDA path."""
     f = np.load(os.path.join(os.path.dirname(__file__), "golden", "decode_compose.npz"))
     tabs = [(f[f"{kk}_idx"], f[f"{kk}_cb"].view(cb3.BF16)) for kk in ("gate", "up", "down")]
-    p = cbmoe.pack_layer(*[table_to_gpu(t) for t in tabs])
+    p = cbmoe.pack_layer(*[table_to_gpu(t) for t in tabs], decode_tables=tables)
     x = f["x"].astype(cb3.BF16)                      # the kernels take bf16 activations
     y = cbmoe.ResidentFetch(path="decode").apply(p, t_bf16(x), torch.from_numpy(f["idx"]).cuda(),
                                                  torch.from_numpy(f["w"]).cuda(), 0, float(f["limit"]))

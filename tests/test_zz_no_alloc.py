@@ -1,4 +1,5 @@
-"""cbmoe_experts_apply_noalloc against cbmoe_experts_apply, through the C ABI (needs a B200: -m gpu).
+"""cbmoe_experts_apply_noalloc against cbmoe_experts_apply and the CPU oracle, through the C ABI (needs a B200:
+-m gpu).
 
 The no-alloc entry point exists for callers that cannot allocate device memory for a workspace (an engine whose
 allocator owns all device memory, a plugin host that forbids allocation during execute, host code that must not
@@ -21,10 +22,10 @@ TOL = 1e-2          # the layer bar every GPU test uses (max |got - want| / max 
 
 
 def _call_noalloc(cbmoe, p, x, idx, w, limit):
-    from cbmoe._lib import Experts, lib, ptr, stream_handle
+    from cbmoe._lib import lib, ptr, stream_handle
+    from cbmoe.resident import _experts_struct
     N, k = idx.shape
-    ex = Experts(p["E"], p["H"], p["I"], p["gate_up_q"][0].data_ptr(), p["gate_up_q"][1].data_ptr(),
-                 p["down_q"][0].data_ptr(), p["down_q"][1].data_ptr())
+    ex = _experts_struct(p)
     y = torch.empty((N, p["H"]), dtype=torch.float32, device="cuda")
     rc = lib().cbmoe_experts_apply_noalloc(ctypes.byref(ex), ptr(x), N, ptr(idx), ptr(w), k, float(limit), ptr(y),
                                            stream_handle())
@@ -41,7 +42,8 @@ def test_noalloc_matches_workspace_entry_point_twice():
                          shared_to_gpu(L["shared"]))
     fetch = cbmoe.ResidentFetch(path="decode")
     for N in (8, 3):                                   # two calls in a row; the second reuses the array's leftovers
-        x = t_bf16(gen.activations(rng, N, H))
+        x_np = gen.activations(rng, N, H)
+        x = t_bf16(x_np)
         idx_np, w_np = gen.routing(rng, N, E, k)
         idx, w = torch.from_numpy(idx_np).cuda(), torch.from_numpy(w_np).cuda()
         want = fetch.apply(p, x, idx, w, 0, gen.LIMIT)
@@ -49,6 +51,9 @@ def test_noalloc_matches_workspace_entry_point_twice():
         assert rc == 0, cbmoe.lib().cbmoe_status_string(rc)
         torch.cuda.synchronize()
         assert moe.max_rel_err(got.cpu().numpy(), want.cpu().numpy()) < TOL
+        # and against the CPU oracle directly, on the same bf16 activations
+        ref = moe.decode_apply(x_np.astype(np.float32), idx_np, w_np, L["gate"], L["up"], L["down"], gen.LIMIT)
+        assert moe.max_rel_err(got.cpu().numpy(), ref) < TOL
     assert cbmoe.device_errors(clear=True) == 0
 
 
