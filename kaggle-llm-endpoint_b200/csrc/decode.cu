@@ -92,16 +92,22 @@ struct Schedule {
   }
 };
 
+// Which items are cut: a cut item pays for partial sums, a device-wide fence and a last-arriver reduction
+// (measured: cutting the last half-grid of items of a config-1 launch cost 10% of the kernel), so only the items of
+// a partial last wave are cut, only when that wave is at most half full and an item is long (>= 12 stages: for the
+// 6-stage items of the config-1 down kernel the cut cost more than the imbalance it removed); with fewer items than
+// CTAs every item is cut (small batches: the pieces spread over the grid).
 __device__ __forceinline__ Schedule make_schedule(const DecodeParams& p, int n_items) {
   Schedule sc;
   sc.n_items = n_items;
   sc.KS = p.KS;
   sc.Q = p.KS < kDecodePieces ? p.KS : kDecodePieces;
   int tail = 0;
-  if (p.part != nullptr && p.done != nullptr && sc.Q > 1) {
-    tail = (int)gridDim.x / 2 > 1 ? (int)gridDim.x / 2 : 1;
+  if (p.part != nullptr && p.done != nullptr && sc.Q > 1 && n_items > 0) {
+    const int G = (int)gridDim.x;
+    const int rem = n_items % G;
+    tail = n_items < G ? n_items : (rem <= G / 2 && p.KS >= 12 ? rem : 0);
     if (tail > p.tail_items) tail = p.tail_items;
-    if (tail > n_items) tail = n_items;
   }
   sc.n_tail = tail;
   sc.n_whole = n_items - tail;
