@@ -31,10 +31,6 @@ import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-# stdout carries exactly one JSON line: NCCL's log (its version banner included) goes to stderr
-os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
-if os.environ.get("NCCL_DEBUG", "").upper() in ("VERSION", "WARN"):
-    del os.environ["NCCL_DEBUG"]
 PKG = os.path.join(ROOT, "kaggle-llm-endpoint_b200")
 for _p in (ROOT, PKG):
     if _p not in sys.path:
@@ -58,10 +54,11 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="resident layers cycled by the steps (profiling "
                     "captures use 1 to keep device memory small)")
-    ap.add_argument("--workload", choices=["decode", "prefill", "ep", "iq"], default="decode",
-                    help="decode = config 1 (the default bench line); prefill = config 3 (4096 tokens, tcgen05 path); "
-                         "ep = config 4 (4 layers, 256 tokens, experts sharded over the GPUs, strong scaling); "
-                         "iq = the config-1 batch on the reference's GGUF IQ table formats (routed experts, 1 GPU)")
+    ap.add_argument("--workload", choices=["decode", "config0", "config2", "prefill", "ep", "iq"], default="decode",
+                    help="decode = config 1 (the default bench line); config0 = one 1024x2048 CB3 matvec (the "
+                         "dequant-matvec GB/s); config2 = 64 Zipf(1.1)-skewed tokens; prefill = config 3 (4096 "
+                         "tokens, tcgen05 path); ep = config 4 (4 layers, 256 tokens, experts sharded over the GPUs, "
+                         "strong scaling); iq = the config-1 batch on the reference's GGUF IQ table formats")
     ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
                     help="N > 1: dispatch/return through peer memory over NVLink, or NCCL send/recv")
     ap.add_argument("--ep-path", choices=["auto", "decode", "grouped"], default="auto",
@@ -491,11 +488,25 @@ def run_ours(args):
                         "sample": f"{n} token(s) of batch 0 of layer 0, one at a time (8 routed experts per token + "
                                   f"shared expert, fp32), C oracle with OpenMP"}
 
+    # ---- config 4 at this N (strong scaling; the EP target), and at N > 1 the multi-GPU parity checks
+    del layers
+    torch.cuda.empty_cache()
+    res4 = config4_measure(args, world, rank, local, dev, group, with_e2e=False)
+    ep_err, dev_bits, tp_err = None, None, None
+    if world > 1:
+        ep_err, dev_bits = ep_parity(world, rank, dev, group, res4)
+        tp_err = tp_parity(world, rank, dev)
+    else:
+        dev_bits = cbmoe.device_errors(clear=True)
+    del res4["layers"]
+
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": config_block(world, args.ep_transport), "clocks": clocks.summary(), "gpu_launches": launches,
+                "config4": config4_block(res4, world), "ep_parity_max_rel_err": ep_err,
+                "tp_parity_max_rel_err": tp_err, "device_errors": dev_bits,
                 "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "ms_per_step": ms_e2e / args.steps},
                 "roofline": roofline,
@@ -672,51 +683,51 @@ def run_prefill(args):
 T_EP, L_EP = 256, 4
 
 
-def run_ep_stack(args):
-    """Config 4: 4 MoE layers of the config-1 shape on 256 tokens (uniform top-8), the 160 experts sharded over the
-    N GPUs (expert parallelism, dispatch and return over NVLink); every rank holds 256/N of the tokens. Strong scaling: the
-    global batch is the same at every N. N = 1 runs the same 4 layers through the single-GPU layer call."""
-    import torch
-    import torch.distributed as dist
-    import cbmoe
-    from cbmoe._lib import launch_count
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    assert T_EP % world == 0 and E % world == 0, (T_EP, E, world)
+def config4_batches(torch, dev, world, rank, n_batches=8):
+    """The same global config-4 batches at every N (one seed): 256 tokens and each layer's uniform top-8 routing;
+    every rank keeps its token rows. Also returns batch 0 whole (for the parity check)."""
     t_loc = T_EP // world
-    group = None
-    layers = []
-    if world > 1:
-        from cbmoe.ep import ExpertParallel
-        group = ExpertParallel(transport=args.ep_transport)
-        for li in range(L_EP):
-            full, _ = make_layer_tables(torch, 3000 + li, dev)
-            layers.append(group.pack_local(*full))
-            del full
-    else:
-        layers = [make_layer(torch, cbmoe, 3000 + li, dev)[0] for li in range(L_EP)]
-    # the same global batches at every N: generated from one seed, each rank keeps its token rows
     g = torch.Generator(device=dev)
     g.manual_seed(11)
-    n_batches = 8
-    batches = []
-    for _ in range(n_batches):
+    batches, whole = [], None
+    for b in range(n_batches):
         x = torch.randn((T_EP, H), device=dev, generator=g).to(torch.bfloat16)
-        routes = []
+        routes, full = [], []
         for _ in range(L_EP):
             logits = torch.randn((T_EP, E), device=dev, generator=g)
             top, idx = torch.topk(logits, TOPK, dim=-1)
             w = torch.softmax(top, dim=-1)
             sl = slice(rank * t_loc, (rank + 1) * t_loc)
             routes.append((idx[sl].to(torch.int32).contiguous(), w[sl].contiguous()))
+            full.append((idx.to(torch.int32).contiguous(), w.contiguous()))
         batches.append((x[rank * t_loc:(rank + 1) * t_loc].contiguous(), routes))
+        if b == 0:
+            whole = (x, full)
+    return batches, whole
+
+
+def config4_measure(args, world, rank, local, dev, group, with_e2e=True, with_kernels=True):
+    """Config 4: 4 MoE layers of the config-1 shape on 256 tokens (uniform top-8), the 160 experts sharded over the
+    N GPUs (expert parallelism, dispatch and return over NVLink); every rank holds 256/N of the tokens. Strong
+    scaling: the global batch is the same at every N. N = 1 runs the same 4 layers through the single-GPU layer call.
+    Device time of exactly K steps between events, max over ranks. Returns the measurements (and the layers)."""
+    import torch
+    import torch.distributed as dist
+    import cbmoe
+    from cbmoe._lib import launch_count
+
+    assert T_EP % world == 0 and E % world == 0, (T_EP, E, world)
+    t_loc = T_EP // world
+    layers = []
+    if group is not None:
+        for li in range(L_EP):
+            full, _ = make_layer_tables(torch, 3000 + li, dev)
+            layers.append(group.pack_local(*full))
+            del full
+    else:
+        layers = [make_layer(torch, cbmoe, 3000 + li, dev)[0] for li in range(L_EP)]
+    batches, whole = config4_batches(torch, dev, world, rank)
+    n_batches = len(batches)
     path = args.ep_path
     fetch = cbmoe.ResidentFetch(path=path)
     cap = ep_capacity(t_loc * TOPK, world)
@@ -759,60 +770,168 @@ def run_ep_stack(args):
     launches = launch_count() - l0
     ms = max_ms(ev0.elapsed_time(ev1))
     barrier()
-    value = T_EP * args.steps / (ms / 1000.0)
+    res = {"value": T_EP * args.steps / (ms / 1000.0), "ms_per_step": ms / args.steps, "launches": launches,
+           "clocks": clocks.summary(), "cap": cap, "path": path, "t_loc": t_loc, "layers": layers,
+           "stack": stack, "whole": whole, "batches": batches}
+    if with_e2e:
+        # this rank's token rows and its 4 layers' routing from pinned host memory, the output back, every step
+        host = [(x.cpu().pin_memory(), [(i.cpu().pin_memory(), w.cpu().pin_memory()) for i, w in r])
+                for x, r in batches]
+        xd = torch.empty((t_loc, H), dtype=torch.bfloat16, device=dev)
+        rd = [(torch.empty((t_loc, TOPK), dtype=torch.int32, device=dev),
+               torch.empty((t_loc, TOPK), dtype=torch.float32, device=dev)) for _ in range(L_EP)]
+        out_h = torch.empty((t_loc, H), dtype=torch.bfloat16).pin_memory()
 
-    # e2e: this rank's token rows and its 4 layers' routing from pinned host memory, the output back, every step
-    host = [(x.cpu().pin_memory(), [(i.cpu().pin_memory(), w.cpu().pin_memory()) for i, w in r]) for x, r in batches]
-    xd = torch.empty((t_loc, H), dtype=torch.bfloat16, device=dev)
-    rd = [(torch.empty((t_loc, TOPK), dtype=torch.int32, device=dev),
-           torch.empty((t_loc, TOPK), dtype=torch.float32, device=dev)) for _ in range(L_EP)]
-    out_h = torch.empty((t_loc, H), dtype=torch.bfloat16).pin_memory()
+        def e2e_step(s):
+            xh, rh = host[s % n_batches]
+            xd.copy_(xh, non_blocking=True)
+            for (i_d, w_d), (i_h, w_h) in zip(rd, rh):
+                i_d.copy_(i_h, non_blocking=True)
+                w_d.copy_(w_h, non_blocking=True)
+            out_h.copy_(stack(xd, rd), non_blocking=True)
 
-    def e2e_step(s):
-        xh, rh = host[s % n_batches]
-        xd.copy_(xh, non_blocking=True)
-        for (i_d, w_d), (i_h, w_h) in zip(rd, rh):
-            i_d.copy_(i_h, non_blocking=True)
-            w_d.copy_(w_h, non_blocking=True)
-        out_h.copy_(stack(xd, rd), non_blocking=True)
+        for s in range(args.warmup):
+            e2e_step(s)
+        barrier()
+        ev0.record()
+        for s in range(args.steps):
+            e2e_step(args.warmup + s)
+        ev1.record()
+        torch.cuda.synchronize()
+        ms_e2e = max_ms(ev0.elapsed_time(ev1))
+        res["e2e"] = {"value": T_EP * args.steps / (ms_e2e / 1000.0), "unit": "tok/s",
+                      "h2d_bytes_per_step": (t_loc * H * 2 + L_EP * t_loc * TOPK * 8) * world,
+                      "d2h_bytes_per_step": t_loc * H * 2 * world, "ms_per_step": ms_e2e / args.steps}
+    if with_kernels:
+        # per-kernel event times (a separate pass: events between kernels), rank 0's view
+        from cbmoe._lib import profile_enable, profile_read
+        profile_read(reset=True)
+        profile_enable(True)
+        for s in range(args.steps):
+            stack(*batches[(args.warmup + s) % n_batches])
+        torch.cuda.synchronize()
+        profile_enable(False)
+        prof = profile_read(reset=True)
+        res["kernels"] = {k: {"launches": n, "avg_us": 1000 * t / n, "ms_per_step": t / args.steps}
+                          for k, (n, t) in prof.items()}
+    return res
 
-    for s in range(args.warmup):
-        e2e_step(s)
-    barrier()
-    ev0.record()
-    for s in range(args.steps):
-        e2e_step(args.warmup + s)
-    ev1.record()
+
+def config4_block(res, world):
+    return {"workload": "config4: 4 MoE layers of the config-1 shape, 256 tokens, uniform top-8, 160 CB3 experts "
+                        "sharded over the GPUs + replicated int8 shared expert (strong scaling)",
+            "value": res["value"], "unit": "tok/s", "ms_per_step": res["ms_per_step"], "n_gpus": world,
+            "global_batch": T_EP, "tokens_per_gpu": res["t_loc"], "experts_per_gpu": E // world,
+            "capacity_rows_per_peer": res["cap"] if world > 1 else None, "path": res["path"],
+            "timing": "device time of K steps between CUDA events, max over ranks", "gpu_launches": res["launches"],
+            "clocks": res["clocks"], "kernels_rank0": res.get("kernels")}
+
+
+def ep_parity(world, rank, dev, group, res):
+    """Layer 0 of the config-4 stack on batch 0 through the expert-parallel layer on every rank; rank 0 gathers the
+    ranks' outputs and compares them with its single-GPU layer call (the whole layer's tables) on the same 256
+    tokens. Returns (max |ep - single| / max |single|, OR of every rank's device error bits); rank 0 only."""
+    import torch
+    import torch.distributed as dist
+    import cbmoe
+    x_full, routes_full = res["whole"]
+    x_loc, routes_loc = res["batches"][0]
+    idx, w = routes_loc[0]
+    out = torch.empty((res["t_loc"], H), dtype=torch.bfloat16, device=dev)
+    group.layer(res["layers"][0], x_loc, idx, w, LIMIT, capacity=res["cap"], out=out, path=res["path"])
+    gathered = [torch.empty_like(out) for _ in range(world)]
+    dist.all_gather(gathered, out)
     torch.cuda.synchronize()
-    ms_e2e = max_ms(ev0.elapsed_time(ev1))
-    e2e = T_EP * args.steps / (ms_e2e / 1000.0)
-    # per-kernel event times (a separate pass: events between kernels), rank 0's view
-    from cbmoe._lib import profile_enable, profile_read
-    profile_read(reset=True)
-    profile_enable(True)
-    for s in range(args.steps):
-        stack(*batches[(args.warmup + s) % n_batches])
-    torch.cuda.synchronize()
-    profile_enable(False)
-    prof = profile_read(reset=True)
-    kern = {k: {"launches": n, "avg_us": 1000 * t / n, "ms_per_step": t / args.steps} for k, (n, t) in prof.items()}
-    h2d = t_loc * H * 2 + L_EP * t_loc * TOPK * 8
-    d2h = t_loc * H * 2
+    errs = torch.tensor([cbmoe.device_errors(clear=True)], dtype=torch.int64, device=dev)
+    allerrs = [torch.empty_like(errs) for _ in range(world)]
+    dist.all_gather(allerrs, errs)
+    bits = 0
+    for e in allerrs:
+        bits |= int(e.item())
+    err = None
     if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        full, _ = make_layer_tables(torch, 3000, dev)
+        p_full = cbmoe.pack_layer(*full)
+        del full
+        want = cbmoe.ResidentFetch(path="auto").layer(p_full, x_full, *routes_full[0], LIMIT).float()
+        got = torch.cat(gathered).float()
+        err = float((got - want).abs().max() / want.abs().max())
+        del p_full
+    dist.barrier()
+    return err, bits
+
+
+def tp_parity(world, rank, dev):
+    """Tensor parallelism over moe_inter (the reference's multi-chip scheme, cbmoe.tp) on a GGUF-format layer (IQ2_S
+    gate/up, IQ3_S down; E = 8, H = 1024, I = 256 per rank): every rank runs all slots on its slice and the partial
+    outputs are all-reduced; rank 0 compares the sum with the whole layer on one GPU. Returns max rel err (rank 0)."""
+    import torch
+    import cbmoe
+    from cbmoe.tp import TensorParallel
+    E_t, H_t, I_t, N_t, k_t = 8, 1024, 256 * world, 16, 4
+    qtypes = {"gate_q": "IQ2_S", "up_q": "IQ2_S", "down_q": "IQ3_S"}
+    shapes = {"gate_q": (I_t, H_t), "up_q": (I_t, H_t), "down_q": (H_t, I_t)}
+    g = torch.Generator(device=dev)
+    g.manual_seed(21)
+
+    def table(qt, rows, K):
+        bb = cbmoe.iq.block_bytes(qt)
+        n = E_t * rows * (K // 256)
+        t = torch.randint(0, 256, (n, bb), dtype=torch.uint8, device=dev, generator=g)
+        d = torch.empty(n, dtype=torch.float16, device=dev).uniform_(1e-3, 2e-2, generator=g)
+        t[:, 0:2] = d.view(torch.uint8).view(n, 2)
+        return t.view(-1)
+
+    tabs = [table(qtypes[k], *shapes[k]) for k in ("gate_q", "up_q", "down_q")]
+    x = torch.randn((N_t, H_t), device=dev, generator=g).to(torch.bfloat16)
+    top, idx = torch.topk(torch.randn((N_t, E_t), device=dev, generator=g), k_t, dim=-1)
+    w = torch.softmax(top, dim=-1)
+    idx = idx.to(torch.int32).contiguous()
+    tp = TensorParallel()
+    p = tp.pack_local(*tabs, qtypes, E_t, H_t, I_t)
+    y = tp.layer(p, x, idx, w, LIMIT)
+    torch.cuda.synchronize()
+    if rank != 0:
+        return None
+    full = cbmoe.iq.pack_layer(*tabs, qtypes, E_t, H_t, I_t)
+    want = cbmoe.iq.apply(full, x, idx, w.contiguous(), LIMIT)
+    return float((y - want).abs().max() / want.abs().max())
+
+
+def run_ep_stack(args):
+    """--workload ep: the config-4 measurement as the line's value (see config4_measure)."""
+    import torch
+    import torch.distributed as dist
+    import cbmoe
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        from cbmoe.ep import ExpertParallel
+        group = ExpertParallel(transport=args.ep_transport)
+    res = config4_measure(args, world, rank, local, dev, group)
+    parity = ep_parity(world, rank, dev, group, res) if world > 1 else (None, None)
+    if rank == 0:
+        line = {"metric": METRIC, "value": res["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": "config4: 4 MoE layers of the config-1 shape, 256 tokens, uniform top-8, "
                                        "160 CB3 experts sharded over the GPUs + replicated int8 shared expert",
-                           "global_batch": T_EP, "tokens_per_gpu": t_loc, "layers": L_EP,
-                           "experts_per_gpu": E // world, "capacity_rows_per_peer": cap if world > 1 else None,
-                           "path": path, "transport": args.ep_transport if world > 1 else None,
+                           "global_batch": T_EP, "tokens_per_gpu": res["t_loc"], "layers": L_EP,
+                           "experts_per_gpu": E // world, "capacity_rows_per_peer": res["cap"] if world > 1 else None,
+                           "path": res["path"], "transport": args.ep_transport if world > 1 else None,
                            "parallelism": f"expert parallel x{world}" if world > 1 else "single GPU",
                            "l2": "4 resident layers (1.47 GB each) per step: inputs larger than L2"},
-                "clocks": clocks.summary(), "gpu_launches": launches,
-                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d * world,
-                        "d2h_bytes_per_step": d2h * world, "ms_per_step": ms_e2e / args.steps},
-                "kernels": kern, "cpu_baseline": None, "device_errors": cbmoe.device_errors(clear=True)}
+                "clocks": res["clocks"], "gpu_launches": res["launches"], "e2e": res["e2e"],
+                "kernels": res["kernels"], "cpu_baseline": None,
+                "ep_parity_max_rel_err": parity[0], "device_errors": parity[1] if world > 1 else
+                cbmoe.device_errors(clear=True)}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -898,8 +1017,285 @@ def run_iq(args):
     print(json.dumps(line))
 
 
+# ------------------------------------------------------------------------------------------------ config 0
+C0_ROWS, C0_K, C0_MATS = 1024, 2048, 256
+C0_BYTES = C0_ROWS * C0_K * 3 // 8 + C0_ROWS * 16 + C0_K * 2 + C0_ROWS * 2      # 808,960: the spec's unit of work
+
+
+def run_config0(args):
+    """Config 0: one CB3 matrix [1024, 2048] (3-bit indices, 8-entry sorted N(0, 0.02) bf16 codebook per row) times
+    one bf16 token. A step = one matvec through the library's decode matvec (cbmoe_cb8_matvec: the activation split
+    plus the int8-digit decode kernel); steps cycle 256 resident matrices (205 MB > L2). value = matvecs (tokens)
+    per second; roofline = the spec's 808,960 bytes per matvec / the decode kernel's event-timed duration."""
+    import ctypes
+    import numpy as np
+    import torch
+    import cbmoe
+    from cbmoe._lib import launch_count, lib, profile_enable, profile_read
+
+    assert int(os.environ.get("WORLD_SIZE", "1")) == 1, "--workload config0 runs on one GPU"
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(17)
+    mats = []
+    for _ in range(C0_MATS):
+        words = torch.randint(0, 256, (C0_ROWS * C0_K * 3 // 32 * 4,), dtype=torch.uint8, device=dev, generator=g)
+        cb = (torch.randn((1, C0_ROWS, 8), device=dev, generator=g) * 0.02).to(torch.bfloat16).float()
+        cb = cb.sort(dim=-1).values.to(torch.bfloat16)
+        idx_k, cb_k = cbmoe.ops.pack_cb3(words.view(torch.int32).view(1, C0_ROWS, C0_K * 3 // 32), cb)
+        mats.append((idx_k, cbmoe.ops.build_cb8(cb_k, 1, 1, C0_ROWS), words, cb))
+    xs = [torch.randn((1, C0_K), device=dev, generator=g).to(torch.bfloat16) for _ in range(64)]
+    y = torch.empty((1, C0_ROWS), dtype=torch.float32, device=dev)
+    ws = torch.empty(lib().cbmoe_cb8_matvec_workspace_bytes(1, C0_K), dtype=torch.uint8, device=dev)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    L = lib()
+
+    def step(s, x=None, out=None):
+        idx_k, cb8, _, _ = mats[s % C0_MATS]
+        xx = xs[s % 64] if x is None else x
+        rc = L.cbmoe_cb8_matvec(ctypes.c_void_p(idx_k.data_ptr()), ctypes.c_void_p(cb8.data_ptr()), C0_ROWS, C0_K,
+                                ctypes.c_void_p(xx.data_ptr()), 1, ctypes.c_void_p((out or y).data_ptr()),
+                                ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream)
+        assert rc == 0, rc
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    # The timed steps replay one CUDA graph of all K steps (each step two kernels: a launch-bound loop, so the host's
+    # launch overhead stays out of the device time); the graph holds the same launches the eager loop makes.
+    cs = torch.cuda.Stream()
+    cs.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    l0 = launch_count()
+    with torch.cuda.stream(cs):
+        stream = ctypes.c_void_p(cs.cuda_stream)
+        with torch.cuda.graph(graph, stream=cs):
+            for s in range(args.steps):
+                step(args.warmup + s)
+    launches = launch_count() - l0
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    graph.replay()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        ev0.record()
+        graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+    ms_step = ev0.elapsed_time(ev1) / args.steps
+    del graph
+    # e2e: the token from pinned host memory, y back, every step (eager launches)
+    xh = [x.cpu().pin_memory() for x in xs[:8]]
+    yh = torch.empty((1, C0_ROWS), dtype=torch.float32).pin_memory()
+    xd = torch.empty((1, C0_K), dtype=torch.bfloat16, device=dev)
+    for s in range(args.warmup):
+        xd.copy_(xh[s % 8], non_blocking=True)
+        step(s, xd)
+        yh.copy_(y, non_blocking=True)
+    torch.cuda.synchronize()
+    ev0.record()
+    for s in range(args.steps):
+        xd.copy_(xh[s % 8], non_blocking=True)
+        step(args.warmup + s, xd)
+        yh.copy_(y, non_blocking=True)
+    ev1.record()
+    torch.cuda.synchronize()
+    ms_e2e = ev0.elapsed_time(ev1) / args.steps
+    profile_read(reset=True)
+    profile_enable(True)
+    for s in range(args.steps):
+        step(args.warmup + s)
+    torch.cuda.synchronize()
+    profile_enable(False)
+    prof = profile_read(reset=True)
+    n_k, t_k = prof["cb3_single"]
+    k_us = 1000.0 * t_k / n_k
+    peak, peak_src = load_peaks()
+    achieved = C0_BYTES / (k_us * 1e-6) / 1e9
+    cpu_baseline = None
+    if not args.no_cpu_baseline:
+        from oracle import cpu
+        cpu.build()
+        _, _, words, cb = mats[0]
+        wnp = words.view(torch.int32).cpu().numpy().view(np.uint32).reshape(C0_ROWS, C0_K * 3 // 32)
+        cbnp = cb[0].view(torch.int16).cpu().numpy().view(np.uint16)
+        xnp = xs[0].float().cpu().numpy()
+        threads = best_threads(cpu, wnp, cbnp)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < min(args.cpu_seconds, 5.0) or n < 3:
+            cpu.cb3_matvec(wnp, cbnp, xnp, threads=threads)
+            n += 1
+        secs = time.perf_counter() - t0
+        cpu_baseline = {"value": n / secs, "unit": "tok/s", "cores": threads, "kind": "port",
+                        "sample": f"{n} matvecs of matrix 0 (fp32, C oracle with OpenMP)"}
+    line = {"metric": METRIC, "value": 1000.0 / ms_step, "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "config0: one CB3 matrix [1024, 2048] (3-bit indices, 8-entry bf16 codebook per "
+                                   "row) x one bf16 token",
+                       "l2": f"{C0_MATS} resident matrices ({C0_MATS * C0_BYTES / 1e6:.0f} MB) cycled: larger than L2",
+                       "path": "cbmoe_cb8_matvec (activation split + int8-digit decode kernel)",
+                       "launch": "value: the K steps replayed as one CUDA graph; e2e: eager launches"},
+            "clocks": clocks.summary(), "gpu_launches": launches,
+            "e2e": {"value": 1000.0 / ms_e2e, "unit": "tok/s", "h2d_bytes_per_step": C0_K * 2,
+                    "d2h_bytes_per_step": C0_ROWS * 4, "ms_per_step": ms_e2e},
+            "roofline": {"bound": "hbm", "kernel": "cb3_single", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": f"{peak_src} hbm_gbs (copy bandwidth)",
+                         "traffic": None, "algorithmic_bytes_per_launch": C0_BYTES, "kernel_avg_us": k_us,
+                         "note": "one launch streams 0.8 MB: bound by launch latency and ramp, not bandwidth"},
+            "kernels": {k: {"launches": n, "avg_us": 1000.0 * t / max(n, 1)} for k, (n, t) in prof.items()},
+            "cpu_baseline": cpu_baseline}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------ config 2
+N_C2 = 64
+
+
+def zipf_batches(torch, dev, seed, n_batches, n_tok):
+    """Config-2 routing: N(0, 1) logits plus a per-expert bias log(E p_r), p_r = r^-1.1 / sum over a seeded random
+    rank permutation r (Zipf(1.1) expert popularity); top-8 by value, softmax over the selected."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    ranks = torch.randperm(E, device=dev, generator=g).double() + 1
+    pz = ranks ** -1.1
+    bias = torch.log(E * pz / pz.sum()).float()
+    out = []
+    for _ in range(n_batches):
+        x = torch.randn((n_tok, H), device=dev, generator=g).to(torch.bfloat16)
+        logits = torch.randn((n_tok, E), device=dev, generator=g) + bias
+        top, idx = torch.topk(logits, TOPK, dim=-1)
+        out.append((x, idx.to(torch.int32).contiguous(), torch.softmax(top, dim=-1).contiguous()))
+    return out
+
+
+def run_config2(args):
+    """Config 2: the config-1 layer on 64 tokens with Zipf(1.1)-skewed routing (hot experts with many tokens, idle
+    ones). Both expert paths are timed (the decode kernels, which AUTO picks at 512 slots, and the grouped tensor-core
+    GEMMs); value = the faster one, which the line names. Steps cycle 16 resident layers and 64 batches."""
+    import numpy as np
+    import torch
+    import cbmoe
+    from cbmoe._lib import launch_count, profile_enable, profile_read
+
+    assert int(os.environ.get("WORLD_SIZE", "1")) == 1, "--workload config2 runs on one GPU"
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    layers, std0 = [], None
+    for li in range(max(1, args.layers)):
+        p, std = make_layer(torch, cbmoe, 1000 + li, dev, keep_std=(li == 0))
+        layers.append(p)
+        std0 = std0 or std
+    batches = zipf_batches(torch, dev, 64, N_BATCHES, N_C2)
+    counts = [torch.bincount(idx.reshape(-1).long(), minlength=E) for _, idx, _ in batches]
+    hist = {"max_tokens_per_expert": float(np.mean([int(c.max()) for c in counts])),
+            "idle_experts": float(np.mean([int((c == 0).sum()) for c in counts])),
+            "distinct_experts": float(np.mean([int((c > 0).sum()) for c in counts])),
+            "slots": N_C2 * TOPK, "note": "means over the 64 batches"}
+    out = torch.empty((N_C2, H), dtype=torch.bfloat16, device=dev)
+
+    def timed(path):
+        fetch = cbmoe.ResidentFetch(path=path)
+
+        def step(s):
+            x, idx, w = batches[s % N_BATCHES]
+            fetch.layer(layers[s % len(layers)], x, idx, w, LIMIT, out=out)
+        for s in range(args.warmup):
+            step(s)
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0 = launch_count()
+        with ClockSampler(0) as clocks:
+            ev0.record()
+            for s in range(args.steps):
+                step(args.warmup + s)
+            ev1.record()
+            torch.cuda.synchronize()
+        launches = launch_count() - l0
+        profile_read(reset=True)
+        profile_enable(True)
+        for s in range(args.steps):
+            step(args.warmup + s)
+        torch.cuda.synchronize()
+        profile_enable(False)
+        return ev0.elapsed_time(ev1) / args.steps, launches, clocks.summary(), profile_read(reset=True), fetch
+
+    runs = {path: timed(path) for path in ("decode", "grouped")}
+    best = min(runs, key=lambda k: runs[k][0])
+    ms_step, launches, clocks, prof, fetch = runs[best]
+    # e2e through the public API with the chosen path
+    host = [(x.cpu().pin_memory(), i.cpu().pin_memory(), w.cpu().pin_memory()) for x, i, w in batches[:8]]
+    xd = torch.empty((N_C2, H), dtype=torch.bfloat16, device=dev)
+    idd = torch.empty((N_C2, TOPK), dtype=torch.int32, device=dev)
+    wd = torch.empty((N_C2, TOPK), dtype=torch.float32, device=dev)
+    out_h = torch.empty((N_C2, H), dtype=torch.bfloat16).pin_memory()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for s in range(args.warmup + args.steps):
+        if s == args.warmup:
+            torch.cuda.synchronize()
+            ev0.record()
+        xh, ih, wh = host[s % 8]
+        xd.copy_(xh, non_blocking=True)
+        idd.copy_(ih, non_blocking=True)
+        wd.copy_(wh, non_blocking=True)
+        fetch.layer(layers[s % len(layers)], xd, idd, wd, LIMIT, out=out)
+        out_h.copy_(out, non_blocking=True)
+    ev1.record()
+    torch.cuda.synchronize()
+    ms_e2e = ev0.elapsed_time(ev1) / args.steps
+    uniq = [float((counts[(args.warmup + s) % N_BATCHES] > 0).sum()) for s in range(args.steps)]
+    S = N_C2 * TOPK
+    u_mean = sum(uniq) / len(uniq)
+    layer_bytes = u_mean * CB3_EXPERT_BYTES + SHARED_BYTES + 2 * N_C2 * H * 2
+    peak, peak_src = load_peaks()
+    roofline = None
+    if best == "decode" and "cb3_gateup" in prof:
+        n, t = prof["cb3_gateup"]
+        gu = u_mean * (2 * I * H * 3 // 8 + 2 * I * 16) + N_C2 * H * 2 + S * I * 4
+        ach = gu / (t / n / 1000.0) / 1e9
+        roofline = {"bound": "hbm", "kernel": "cb3_gateup", "achieved": ach, "peak": peak, "unit": "GB/s",
+                    "frac": ach / peak, "peak_source": f"{peak_src} hbm_gbs (copy bandwidth)", "traffic": None,
+                    "algorithmic_bytes_per_launch": gu}
+    cpu_baseline = None
+    if not args.no_cpu_baseline:
+        from oracle import cpu
+        cpu.build()
+        std_np = std_to_numpy(std0)
+        x, idx, w = batches[0]
+        threads = best_threads(cpu, std_np["down"][0][int(idx[0, 0])], std_np["down"][1][int(idx[0, 0])])
+        n, secs = cpu_layer_sample(std_np, x.float().cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(),
+                                   args.cpu_seconds, threads)
+        cpu_baseline = {"value": n / secs, "unit": "tok/s", "cores": threads, "kind": "port",
+                        "sample": f"{n} token(s) of batch 0 of layer 0, one at a time (C oracle with OpenMP)"}
+    line = {"metric": METRIC, "value": N_C2 * 1000.0 / ms_step, "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "config2: MoE layer, 64 tokens, Zipf(1.1)-skewed routing, E=160 CB3 routed + int8 "
+                                   "shared, H=5120, I=1536, top-8",
+                       "path": best, "paths_ms_per_step": {k: v[0] for k, v in runs.items()},
+                       "token_histogram": hist,
+                       "l2": "16 resident layers (1.47 GB each) cycled: inputs larger than L2"},
+            "clocks": clocks, "gpu_launches": launches,
+            "e2e": {"value": N_C2 * 1000.0 / ms_e2e, "unit": "tok/s", "h2d_bytes_per_step": N_C2 * (H * 2 + TOPK * 8),
+                    "d2h_bytes_per_step": N_C2 * H * 2, "ms_per_step": ms_e2e},
+            "roofline": roofline,
+            "layer": {"gbs": layer_bytes / (ms_step / 1000.0) / 1e9,
+                      "frac_of_peak": layer_bytes / (ms_step / 1000.0) / 1e9 / peak,
+                      "algorithmic_bytes_per_step": layer_bytes, "distinct_experts_per_step": u_mean},
+            "kernels": {k: {"launches": n, "avg_us": 1000.0 * t / max(n, 1)} for k, (n, t) in prof.items()},
+            "cpu_baseline": cpu_baseline, "device_errors": cbmoe.device_errors(clear=True)}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.workload == "config0" and args.impl == "ours":
+        run_config0(args)
+        return
+    if args.workload == "config2" and args.impl == "ours":
+        run_config2(args)
+        return
     if args.workload == "iq" and args.impl == "ours":
         run_iq(args)
         return

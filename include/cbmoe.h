@@ -172,8 +172,8 @@ size_t cbmoe_matvec_workspace_bytes(int N);
 int cbmoe_cb3_matvec(const void* idx_k, const void* cb_k, int rows, int K, const uint16_t* x, int N, float* y,
                      void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
-/* cbmoe_cb3_matvec on CB8 tables (cbmoe_cb8_build): the same product through the e4m3 decode kernel. The
- * workspace (cbmoe_cb8_matvec_workspace_bytes, 16-byte aligned) holds the split activations. */
+/* cbmoe_cb3_matvec on CB8 tables (cbmoe_cb8_build): the same product through the int8-digit decode kernel. The
+ * workspace (cbmoe_cb8_matvec_workspace_bytes, 16-byte aligned) holds the split activations. K <= 65536. */
 size_t cbmoe_cb8_matvec_workspace_bytes(int N, int K);
 int cbmoe_cb8_matvec(const void* idx_k, const void* cb8, int rows, int K, const uint16_t* x, int N, float* y,
                      void* workspace, size_t workspace_bytes, cudaStream_t stream);
@@ -182,6 +182,15 @@ int cbmoe_cb8_matvec(const void* idx_k, const void* cb8, int rows, int K, const 
  * y fp32 [N, rows] = x @ bf16(q * s). Workspace: cbmoe_matvec_workspace_bytes. */
 int cbmoe_w8_linear(const void* qk, const float* s, int scale_axis, int rows, int K, const uint16_t* x, int N,
                     float* y, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* The int8 lm_head (engine.py:345-351 `_logits_local` with int8 columns): logits bf16 [N, rows] =
+ * bf16(f32(x @ q) * s), the scale applied after the dot, per output column: q int8 [K, rows] as quantize_array makes
+ * it with per-column scales s fp32 [rows] (scale_axis 1), in the W8K layout (cbmoe_w8k_repack, nmat 1); x bf16
+ * [N, K]. The stored int8 weights are multiplied as they are against x split into two int8 digits per element
+ * (exact int32 sums; exact for bf16 within 2^6 of the token's largest |x|). Workspace:
+ * cbmoe_cb8_matvec_workspace_bytes(N, K), 16-byte aligned. K <= 65536. */
+int cbmoe_w8_logits(const void* qk, const float* s, int rows, int K, const uint16_t* x, int N, uint16_t* out,
+                    void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /* -------------------------------------------------------------------------------- expert parallelism
  * Routed experts sharded by id over the ranks of one node (rank r holds experts [r*E/n, (r+1)*E/n)); tokens stay on

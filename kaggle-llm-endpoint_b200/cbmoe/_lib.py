@@ -81,6 +81,8 @@ SIGNATURES = {
                                  c_void_p]),
     "cbmoe_w8_linear": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                 c_size_t, c_void_p]),
+    "cbmoe_w8_logits": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_size_t,
+                                c_void_p]),
     "cbmoe_route": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_void_p,
                             c_void_p, c_void_p]),
     "cbmoe_iq_block_bytes": (c_size_t, [c_int]),

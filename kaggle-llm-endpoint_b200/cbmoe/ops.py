@@ -142,3 +142,18 @@ def w8_linear(qk, s, scale_axis, rows, K, x):
     check(lib().cbmoe_w8_linear(ptr(qk), ptr(_contig(s, torch.float32)), scale_axis, rows, K, ptr(x), N, ptr(y),
                                 None, 0, stream_handle()), "cbmoe_w8_linear")
     return y
+
+
+def w8_logits(qk, s, rows, K, x, ws=None):
+    """The int8 lm_head (engine.py:345-351): x bf16 [N, K] times int8 columns (W8K, per-column scales s [rows])
+    -> bf16 [N, rows] = bf16(f32(x @ q) * s), the scale after the dot."""
+    require_cuda(qk, s, x)
+    N = x.shape[0]
+    xb = x.to(torch.bfloat16).contiguous()
+    out = torch.empty((N, rows), dtype=torch.bfloat16, device=x.device)
+    if ws is None:
+        ws = torch.empty(max(1, lib().cbmoe_cb8_matvec_workspace_bytes(N, K)), dtype=torch.uint8, device=x.device)
+    check(lib().cbmoe_w8_logits(ptr(qk), ptr(s.float().contiguous()), rows, K, ptr(xb), N, ptr(out), ptr(ws),
+                                ws.numel(), stream_handle()), "cbmoe_w8_logits")
+    return out
+

@@ -406,6 +406,14 @@ using namespace lyr;
 
 void set_last_cuda_error(cudaError_t e) { t_last_cuda_error = (int)e; }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("CBMOE_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 int num_sms() {
   static int cached[64] = {0};
   int dev = 0;
@@ -584,7 +592,8 @@ extern "C" size_t cbmoe_cb8_matvec_workspace_bytes(int N, int K) {
 
 extern "C" int cbmoe_cb8_matvec(const void* idx_k, const void* cb8, int rows, int K, const uint16_t* x, int N,
                                 float* y, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  if (!idx_k || !cb8 || rows <= 0 || K <= 0 || rows % kRowsPerBlock || K % kStageK || N < 0) return CBMOE_ERR_INVALID;
+  if (!idx_k || !cb8 || rows <= 0 || K <= 0 || rows % kRowsPerBlock || K % kStageK || K > 65536 || N < 0)
+    return CBMOE_ERR_INVALID;
   if (N > 0 && (!x || !y || !aligned16(x) || !aligned16(idx_k) || !aligned16(cb8))) return CBMOE_ERR_INVALID;
   if (N == 0) return CBMOE_OK;
   if (!workspace || workspace_bytes < cbmoe_cb8_matvec_workspace_bytes(N, K) || !aligned16(workspace))
@@ -605,6 +614,34 @@ extern "C" int cbmoe_cb8_matvec(const void* idx_k, const void* cb8, int rows, in
   p.N = N;
   p.y_out = y;
   return decode_cb8_single(p, N <= 4 ? 1 : 2, stream);
+}
+
+extern "C" int cbmoe_w8_logits(const void* qk, const float* s, int rows, int K, const uint16_t* x, int N,
+                               uint16_t* out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!qk || !s || rows <= 0 || K <= 0 || rows % kRowsPerBlock || K % kStageK || K > 65536 || N < 0 ||
+      !aligned16(s))
+    return CBMOE_ERR_INVALID;
+  if (N > 0 && (!x || !out || !aligned16(x) || !aligned16(qk))) return CBMOE_ERR_INVALID;
+  if (N == 0) return CBMOE_OK;
+  if (!workspace || workspace_bytes < cbmoe_cb8_matvec_workspace_bytes(N, K) || !aligned16(workspace))
+    return CBMOE_ERR_WORKSPACE;
+  uint8_t* x8 = static_cast<uint8_t*>(workspace);
+  float* xs = reinterpret_cast<float*>(x8 + align_up((size_t)N * K * 2));
+  int rc = launch_split_x(x, N, K, x8, xs, stream);
+  if (rc) return rc;
+  DecodeParams p = base_params();
+  p.wq = static_cast<const uint8_t*>(qk);
+  p.s0 = s;
+  p.scale_axis = 1;
+  p.rows = rows;
+  p.K = K;
+  p.RB = rows / kRowsPerBlock;
+  p.KS = K / kStageK;
+  p.b8 = x8;
+  p.b8_scale = xs;
+  p.N = N;
+  p.y_bf16 = out;
+  return decode_w8i_logits(p, N <= 4 ? 1 : 2, stream);
 }
 
 extern "C" int cbmoe_w8_linear(const void* qk, const float* s, int scale_axis, int rows, int K, const uint16_t* x,

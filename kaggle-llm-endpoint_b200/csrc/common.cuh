@@ -161,6 +161,30 @@ namespace cbmoe {
 void set_last_cuda_error(cudaError_t e);
 int num_sms();
 
+// Programmatic dependent launch: a kernel launched this way may start (launch, CTA placement, shared-memory set-up)
+// while its predecessor on the stream is finishing; griddep_wait() then blocks until the predecessor has completed
+// and its writes are visible, so every kernel of this library calls it before its first global-memory access.
+// (In a kernel launched without the attribute it returns at once.) griddep_launch() lets the successor start being
+// placed. CBMOE_PDL=0 in the environment launches everything plainly (a measurement switch).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // One-time set-up per device (a kernel's shared-memory attribute, its resident grid): `init(value)` runs once for
 // each device, with that device current, under a lock; on success (CBMOE_OK) the value it set is kept for that
 // device. Kernel attributes are per device, so a process that drives several GPUs sets them on each.

@@ -28,10 +28,14 @@ struct Fmt<kFmtCB8A> {
 };
 template <int FMT>
 constexpr bool is_cb8() { return FMT == kFmtCB8 || FMT == kFmtCB8A; }
+// Formats multiplied on the int8 tensor-core MMA against split activations (X8 / H8 rows): CB8 (table lookups into
+// int8 / uint8 bytes) and W8I (the stored int8 weights as they are).
+template <int FMT>
+constexpr bool is_split() { return is_cb8<FMT>() || FMT == kFmtW8I; }
 
 template <int FMT, int NMAT, int NT, int HILO, int NSTAGE>
 struct DecodeSmem {
-  static constexpr bool kCb8 = is_cb8<FMT>();
+  static constexpr bool kCb8 = is_split<FMT>();
   static constexpr int kUnit = Fmt<FMT>::kUnitBytes;
   static constexpr int kWBytes = kConsumerWarps * NMAT * kUnit;
   // codebooks (CB3K), tables + row factors (CB8) or scales (W8K) of the item
@@ -149,7 +153,7 @@ __device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, %0;" 
 #endif
 template <int FMT, int NT, int HILO>
 constexpr int decode_min_blocks() {
-  if constexpr (is_cb8<FMT>()) return (NT == (HILO ? 2 : 1)) ? CBMOE_CB8_MINB_SMALL : 3;
+  if constexpr (is_split<FMT>()) return (NT == (HILO ? 2 : 1)) ? CBMOE_CB8_MINB_SMALL : 3;
   return NT == 1 ? CBMOE_DECODE_MINB_NT1 : 1;
 }
 
@@ -157,7 +161,8 @@ template <int FMT, int NMAT, int NT, int EPI, int HILO, int NSTAGE>
 __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<FMT, NT, HILO>())
     decode_kernel_t(const DecodeParams p) {
   using SM = DecodeSmem<FMT, NMAT, NT, HILO, NSTAGE>;
-  constexpr bool kCb8 = SM::kCb8;
+  constexpr bool kCb8 = SM::kCb8;          // split activations, int8 MMA (CB8 or W8I)
+  constexpr bool kW8I = FMT == kFmtW8I;
   constexpr int kPassTokens = SM::kPassTokens;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -175,6 +180,7 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<FMT, NT, HIL
     fence_mbar_init();
   }
   __syncthreads();
+  griddep_wait();   // the plan / the previous expert kernel's output is complete past this point
 
   const int n_items = count_items(p, kPassTokens);
   const int RB = p.RB, KS = p.KS;
@@ -262,7 +268,7 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<FMT, NT, HIL
           if (aux > 0 && lane < NMAT) {
             if constexpr (FMT == kFmtCB3) {
               if (lane == 0) bulk_g2s(sa, p.cb + cb_offset_words(pi.e, rb, 0, 0, 0, RB, NMAT), aux, &full[st]);
-            } else if constexpr (kCb8) {
+            } else if constexpr (kCb8 && !kW8I) {
               if (lane == 0) bulk_g2s(sa, p.cb8 + cb8_block_offset(pi.e, rb, RB, NMAT), aux, &full[st]);
             } else {
               const float* scl = (lane == 0) ? p.s0 : p.s1;
@@ -299,6 +305,7 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<FMT, NT, HIL
       hdr[st].item = -1;
       mbar_arrive(&full[st]);
     }
+    if (lane == 0) griddep_launch();   // no more copies from this CTA: the next kernel may start being placed
     return;
   }
 
@@ -357,9 +364,15 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<FMT, NT, HIL
           const float h0 = (acc[0][n][2] + acc[0][n][3] * 256.f) * fx;
           if constexpr (EPI == kEpiStore) {
             if (j < e.cnt) {
-              float* y = p.y_out + (size_t)(e.row0 + j) * p.rows + rowbase + g;
-              y[0] = g0;
-              y[8] = h0;
+              const size_t o = (size_t)(e.row0 + j) * p.rows + rowbase + g;
+              if (p.y_bf16 != nullptr) {
+                const __nv_bfloat16 b0 = __float2bfloat16_rn(g0), b1 = __float2bfloat16_rn(h0);
+                p.y_bf16[o] = *reinterpret_cast<const uint16_t*>(&b0);
+                p.y_bf16[o + 8] = *reinterpret_cast<const uint16_t*>(&b1);
+              } else {
+                p.y_out[o] = g0;
+                p.y_out[o + 8] = h0;
+              }
             }
           } else {
             // SwiGLU, then h as 4 signed base-256 digits with one factor per (token, 64-row block): the block's
@@ -487,7 +500,7 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<FMT, NT, HIL
           cbg[m] = {ca.x, ca.y, ca.z, ca.w};
           cbh[m] = {cb.x, cb.y, cb.z, cb.w};
           sg[m] = sh[m] = 0.f;
-        } else if constexpr (kCb8) {
+        } else if constexpr (kCb8 && !kW8I) {
           const uint4 ca = lds128(sa + ((warp * NMAT + m) * 16 + g) * 16);
           const uint4 cb = lds128(sa + ((warp * NMAT + m) * 16 + g + 8) * 16);
           c8g[m] = {ca.x, ca.y, ca.z, ca.w};
@@ -513,7 +526,7 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<FMT, NT, HIL
     }
 
     uint32_t wd[NMAT][12];
-    if constexpr (FMT == kFmtCB3 || kCb8) {
+    if constexpr (FMT == kFmtCB3 || (kCb8 && !kW8I)) {
 #pragma unroll
       for (int m = 0; m < NMAT; ++m) {
         const uint8_t* u = sw + (warp * NMAT + m) * SM::kUnit + lane * 48;
@@ -545,8 +558,25 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<FMT, NT, HIL
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) {
           uint32_t ah[2][4], al[2][4];
-          cb8_dequant_chunk<FMT == kFmtCB8 ? CBMOE_CB8_FMA_MODE : 0>(wd[m][3 * c], wd[m][3 * c + 1],
-                                                                      wd[m][3 * c + 2], c8g[m], c8h[m], p.sel, ah, al);
+          if constexpr (kW8I) {
+            // the lane's 16 stored int8 weights of rows g and g+8 in this chunk: 8 per k32 step, as the fragment wants
+            const uint8_t* u = sw + (warp * NMAT + m) * SM::kUnit;
+            const uint4 qg = lds128(u + ((c * 2 + 0) * 32 + lane) * 16);
+            const uint4 qh = lds128(u + ((c * 2 + 1) * 32 + lane) * 16);
+            ah[0][0] = qg.x; ah[0][1] = qh.x; ah[0][2] = qg.y; ah[0][3] = qh.y;
+            ah[1][0] = qg.z; ah[1][1] = qh.z; ah[1][2] = qg.w; ah[1][3] = qh.w;
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+              if (!(n == 0 || n * SM::kTokPerTile < h.cnt)) continue;
+              mma_i8<false>(ci_hi[m][n], ah[0], bx[n].x, bx[n].y);
+              mma_i8<false>(ci_hi[m][n], ah[1], bx[n].z, bx[n].w);
+            }
+            continue;
+          } else {
+            cb8_dequant_chunk<FMT == kFmtCB8 ? CBMOE_CB8_FMA_MODE : 0>(wd[m][3 * c], wd[m][3 * c + 1],
+                                                                        wd[m][3 * c + 2], c8g[m], c8h[m], p.sel, ah,
+                                                                        al);
+          }
 #pragma unroll
           for (int n = 0; n < NT; ++n) {
             if (!(n == 0 || n * SM::kTokPerTile < h.cnt)) continue;
@@ -645,7 +675,9 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<FMT, NT, HIL
         for (int n = 0; n < NT; ++n)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const float v = (HILO ? acc[m][n][i] : (float)ci_hi[m][n][i] * 256.f + (float)ci_lo[m][n][i]);
+            const float v = HILO  ? acc[m][n][i]
+                            : kW8I ? (float)ci_hi[m][n][i]
+                                   : (float)ci_hi[m][n][i] * 256.f + (float)ci_lo[m][n][i];
             acc[m][n][i] = v * ((i & 2) ? sh[m] : sg[m]);
           }
     }
@@ -683,6 +715,8 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<FMT, NT, HIL
 __global__ void combine_kernel(const float* __restrict__ y_sorted, const int* __restrict__ row_slot,
                                const float* __restrict__ wts, int N, int topk, int H, const float* __restrict__ add,
                                float* __restrict__ out_f32, uint16_t* __restrict__ out_bf16) {
+  griddep_wait();
+  griddep_launch();
   const int H4 = H / 4;
   const long long total = (long long)N * H4;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -746,7 +780,7 @@ int launch_decode_t(const DecodeParams& p, int kind, cudaStream_t stream) {
   if (rc) return rc;
   const int g = (p.grid_cap > 0 && p.grid_cap < grid) ? p.grid_cap : (int)grid;
   prof_begin(kind, stream);
-  kern<<<g, kDecodeThreads, SM::kTotal, stream>>>(p);
+  CBMOE_CUDA_TRY(launch_pdl(kern, dim3(g), dim3(kDecodeThreads), SM::kTotal, stream, p));
   prof_end(kind, stream);
   CBMOE_CUDA_TRY(cudaGetLastError());
   return CBMOE_OK;
@@ -778,7 +812,8 @@ int launch_combine(const float* y_sorted, const int* row_slot, const float* wts,
   if (blocks > num_sms() * 8) blocks = num_sms() * 8;
   if (blocks < 1) blocks = 1;
   prof_begin(kProfCombine, stream);
-  combine_kernel<<<blocks, 256, 0, stream>>>(y_sorted, row_slot, wts, N, topk, H, add, out_f32, out_bf16);
+  CBMOE_CUDA_TRY(launch_pdl(combine_kernel, dim3(blocks), dim3(256), 0, stream, y_sorted, row_slot, wts, N, topk, H,
+                            add, out_f32, out_bf16));
   prof_end(kProfCombine, stream);
   CBMOE_CUDA_TRY(cudaGetLastError());
   return CBMOE_OK;
@@ -826,6 +861,9 @@ int decode_cb8_down(const DecodeParams& p, int nt, cudaStream_t s) {
   return cb8_fmt() == kFmtCB8 ? launch_cb8_nt<kFmtCB8, 1, kEpiStore, 1>(p, nt, kProfCb3Down, s)
                               : launch_cb8_nt<kFmtCB8A, 1, kEpiStore, 1>(p, nt, kProfCb3Down, s);
 }
+int decode_w8i_logits(const DecodeParams& p, int nt, cudaStream_t s) {
+  return launch_cb8_nt<kFmtW8I, 1, kEpiStore, 0>(p, nt, kProfW8Single, s);
+}
 int decode_cb8_single(const DecodeParams& p, int nt, cudaStream_t s) {
   return cb8_fmt() == kFmtCB8 ? launch_cb8_nt<kFmtCB8, 1, kEpiStore, 0>(p, nt, kProfCb3Single, s)
                               : launch_cb8_nt<kFmtCB8A, 1, kEpiStore, 0>(p, nt, kProfCb3Single, s);
@@ -834,6 +872,8 @@ int decode_cb8_single(const DecodeParams& p, int nt, cudaStream_t s) {
 __global__ void split_x_kernel(const uint16_t* __restrict__ x, int N, int K, uint8_t* __restrict__ x8,
                                float* __restrict__ scale) {
   __shared__ float red[32];
+  griddep_wait();
+  griddep_launch();
   for (int r = blockIdx.x; r < N; r += gridDim.x)
     split_x_row(x + (size_t)r * K, K, x8 + (size_t)r * (K / kStageK) * kX8StageBytes, scale + r, red);
 }
@@ -842,7 +882,7 @@ int launch_split_x(const uint16_t* x, int N, int K, uint8_t* x8, float* scale, c
   if (N <= 0) return CBMOE_OK;
   const int blocks = N < num_sms() * 4 ? N : num_sms() * 4;
   prof_begin(kProfOther, stream);
-  split_x_kernel<<<blocks, 256, 0, stream>>>(x, N, K, x8, scale);
+  CBMOE_CUDA_TRY(launch_pdl(split_x_kernel, dim3(blocks), dim3(256), 0, stream, x, N, K, x8, scale));
   prof_end(kProfOther, stream);
   CBMOE_CUDA_TRY(cudaGetLastError());
   return CBMOE_OK;

@@ -33,6 +33,7 @@ struct DecodeParams {
   uint16_t* h_out;          // SWIGLU: [sorted row][2*rows] (per 256 block: hi 256 | lo 256)
   uint8_t* h8_out;          // CB8 SWIGLU: H8 rows [sorted row][rows/256][1040 B]
   float* y_out;             // STORE: [row][rows]
+  uint16_t* y_bf16;         // STORE with X8 rows: bf16 [row][rows] instead of y_out (the int8 lm_head)
   // work distribution (decode.cu, Schedule): tickets over whole items, then over pieces of the tail items
   int grid_cap;             // CTAs to launch at most (0: the resident grid)
   int* sched;               // [0] = ticket counter, zero at launch (nullptr: static round-robin over tickets)
@@ -53,6 +54,8 @@ inline size_t decode_part_bytes(int tail_items, int nt, int nmat) {
 int decode_cb8_gateup(const DecodeParams& p, int nt, cudaStream_t s);
 int decode_cb8_down(const DecodeParams& p, int nt, cudaStream_t s);
 int decode_cb8_single(const DecodeParams& p, int nt, cudaStream_t s);
+// int8 leaves (W8K, per-output-column scales) times X8 rows, bf16 out: the int8 lm_head (nt: token tiles of 4).
+int decode_w8i_logits(const DecodeParams& p, int nt, cudaStream_t s);
 // X8 rows of N bf16 rows of K inputs (K % 256 == 0): x8 [N][K/256][512 B], scale [N].
 int launch_split_x(const uint16_t* x, int N, int K, uint8_t* x8, float* scale, cudaStream_t stream);
 int decode_cb3_gateup(const DecodeParams& p, int nt, cudaStream_t s);

@@ -56,6 +56,7 @@ constexpr int kW8kUnitBytes = 4 * 2 * 32 * 16;                // 4096
 constexpr int kFmtCB3 = 0;
 constexpr int kFmtW8 = 1;
 constexpr int kFmtCB8 = 2;
+constexpr int kFmtW8I = 4;   // int8 leaves (W8K) multiplied as stored against X8 digits: the int8 lm_head
 constexpr int kCb8RowBytes = 16 + 4;                           // tables + row factor
 constexpr int kCb8BlockBytes = kRowsPerBlock * kCb8RowBytes;   // per matrix and 64-row block: 1280
 constexpr int kX8StageBytes = 4 * 2 * 64;                      // 512
@@ -74,6 +75,10 @@ struct Fmt<kFmtW8> {
 template <>
 struct Fmt<kFmtCB8> {
   static constexpr int kUnitBytes = kCb3kUnitBytes;   // the CB3K index bits
+};
+template <>
+struct Fmt<kFmtW8I> {
+  static constexpr int kUnitBytes = kW8kUnitBytes;
 };
 
 struct Codebook {

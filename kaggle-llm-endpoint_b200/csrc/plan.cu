@@ -66,6 +66,8 @@ __global__ void __launch_bounds__(kPlanThreads) route_plan_kernel(const int32_t*
                                                                   int tm, int pass_tokens, int32_t* __restrict__ plan,
                                                                   PlanLayout L, int* __restrict__ zero, int n_zero,
                                                                   SplitX split) {
+  griddep_wait();     // the previous layer's kernels may still read the plan buffer until here
+  griddep_launch();
   if (blockIdx.x > 0) {
     __shared__ float s_red[32];
     const int KS = split.K / kStageK;
@@ -500,8 +502,8 @@ int launch_route_plan(const int32_t* idx, const float* w, int T, int k, int E, i
   prof_begin(kProfPlan, stream);
   int blocks = 1;
   if (sx.x8 != nullptr) blocks += sx.N < num_sms() * 2 ? sx.N : num_sms() * 2;
-  route_plan_kernel<<<blocks, kPlanThreads, smem, stream>>>(idx, w, T, k, E, tm, pass_tokens, plan, L, zero, n_zero,
-                                                            sx);
+  CBMOE_CUDA_TRY(launch_pdl(route_plan_kernel, dim3(blocks), dim3(kPlanThreads), smem, stream, idx, w, T, k, E, tm,
+                            pass_tokens, plan, L, zero, n_zero, sx));
   prof_end(kProfPlan, stream);
   CBMOE_CUDA_TRY(cudaGetLastError());
   return CBMOE_OK;

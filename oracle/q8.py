@@ -31,3 +31,12 @@ def dequant(q: np.ndarray, s: np.ndarray) -> np.ndarray:
 def matmul(x: np.ndarray, q: np.ndarray, s: np.ndarray) -> np.ndarray:
     """x [..., in] @ dequant(q, s) [in, out] in float64 -> [..., out]."""
     return np.asarray(x, np.float64) @ dequant(q, s).astype(np.float64)
+
+
+def logits_colscale(h, q, s):
+    """The int8 lm_head of engine.py:345-351 (`_logits_local`): bf16(f32(h @ bf16(q)) * s), the per-column scale
+    s [1, V] applied after the dot; h bf16 [..., D], q int8 [D, V]. The dot in float64 (exact at these sizes), the
+    scaling and the rounding in float32, as the reference scales its f32 result and casts it to bf16."""
+    z = (np.asarray(h, BF16).astype(np.float64) @ np.asarray(q).astype(np.float64)).astype(np.float32)
+    return (z * np.asarray(s, np.float32)).astype(BF16)
+

@@ -15,6 +15,7 @@ Executed reference functions (paths relative to launcher/glm53-flash/engine/glm5
   quant8.py      quantize_array, is_q8, dequant_tree  -> quant8.npz
   resident.py    ResidentFetch._apply_kernel          -> decode_compose.npz  (kernel calls stubbed, see below)
   resident.py    ResidentFetch._apply_ragged_kernel   -> ragged_compose_*.npz
+  engine.py      Engine._logits_local (int8 columns) -> logits_q8.npz (the int8 lm_head: scale after the dot)
 For the two compositions the Pallas kernels (`moe_matvec`, `moe_ragged_gateup/down`) and the GGUF plane helpers are
 replaced by CB3 stand-ins (exact dequant + f32 contraction, bf16 rounding where the kernels round); what the fixture
 pins is the reference's composition around them: slot repetition, swiglu, the weighted combine, the ragged plan,
@@ -235,10 +236,34 @@ def gen_compositions():
                  **tabs)
 
 
+def gen_logits():
+    quantize_array = ref_function("quant8.py", "quantize_array")
+    is_q8 = ref_function("quant8.py", "is_q8", extra={"Q8_KEYS": frozenset({"q", "s"})})
+    q8mod = types.ModuleType("glm53.quant8")
+    q8mod.is_q8 = is_q8
+    pkg = types.ModuleType("glm53")
+    pkg.quant8 = q8mod
+    sys.modules.setdefault("glm53", pkg)
+    sys.modules.setdefault("glm53.quant8", q8mod)
+    logits_local = ref_function("engine.py", "_logits_local", cls="Engine")
+    rng = np.random.default_rng(15)
+    D, V, B = 512, 384, 5
+    w = (rng.standard_normal((D, V)) * 0.02).astype(np.float32)
+    w[:, 7] = 0.0                                          # a zero column: scale at the 1e-12 floor
+    qd = quantize_array(J(w), 1)                           # per-column scales [1, V], as the lm_head leaf
+    h = rng.standard_normal((B, D)).astype(np.float32)
+    h[1] *= 30.0                                           # a token with a large range
+    hb = h.astype(ml_dtypes.bfloat16)
+    z = logits_local(None, {"q": qd["q"], "s": qd["s"]}, J(hb))
+    np.savez(os.path.join(HERE, "logits_q8.npz"), h=hb.view(np.uint16), q=np.asarray(qd["q"]),
+             s=np.asarray(qd["s"], np.float32), z=np.asarray(z).view(np.uint16))
+
+
 if __name__ == "__main__":
     assert os.path.isdir(ENGINE), f"reference engine not found at {ENGINE!r}: set CBMOE_REFERENCE"
     gen_plans()
     gen_swiglu()
     gen_quant8()
     gen_compositions()
+    gen_logits()
     print("golden fixtures written to", HERE)

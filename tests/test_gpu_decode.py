@@ -286,3 +286,40 @@ def test_empty_batch(cbmoe):
     y = cbmoe.ResidentFetch(path="decode").apply(p, x, torch.zeros((0, 8), dtype=torch.int32, device="cuda"),
                                                   torch.zeros((0, 8), device="cuda"), 0, gen.LIMIT)
     assert y.shape == (0, H)
+
+
+def test_w8_logits_reference_fixture(cbmoe):
+    """The int8 lm_head kernel against the reference's `Engine._logits_local` (int8 columns, executed by
+    tests/golden/make_golden.py): within one bf16 unit in the last place (the sums run in another order)."""
+    f = np.load(os.path.join(os.path.dirname(__file__), "golden", "logits_q8.npz"))
+    q, s = f["q"], f["s"].reshape(-1)
+    D, V = q.shape
+    qk = cbmoe.ops.pack_w8(torch.from_numpy(q).cuda())
+    h = torch.from_numpy(f["h"].view(np.int16).copy()).cuda().view(torch.bfloat16)
+    got = cbmoe.ops.w8_logits(qk, torch.from_numpy(s).cuda(), V, D, h).float().cpu().numpy()
+    want = f["z"].view(cb3.BF16).astype(np.float32)
+    assert np.all(np.abs(got - want) <= _logit_tol(want))
+    assert np.mean(got == want) > 0.9
+    _no_device_errors(cbmoe)
+
+
+def _logit_tol(want):
+    """One bf16 unit in the last place of each logit, plus 2^-12 of its row's largest: a logit that nearly cancels
+    carries the summation order's rounding (the reference sums in f32, the kernel exactly in int32) at the scale of
+    its terms, not of its own value."""
+    return np.abs(want) * 2.0 ** -7 + np.abs(want).max(axis=-1, keepdims=True) * 2.0 ** -12
+
+
+@pytest.mark.parametrize("B", [1, 8, 13])
+def test_w8_logits_lm_head_shape(cbmoe, B):
+    """[B, 5120] x [5120, V/8] (V = 151552: one GPU's vocab columns of an 8-way split) against the oracle's
+    bf16(f32(h @ q) * s): within one bf16 unit in the last place."""
+    D, V = 5120, 151552 // 8
+    rng = np.random.default_rng(B)
+    q, s = gen.q8_leaf(rng, D, V, 1)
+    h = gen.activations(rng, B, D)
+    qk = cbmoe.ops.pack_w8(torch.from_numpy(q).cuda())
+    got = cbmoe.ops.w8_logits(qk, torch.from_numpy(s.reshape(-1)).cuda(), V, D, t_bf16(h)).float().cpu().numpy()
+    want = q8.logits_colscale(h, q, s).astype(np.float32)
+    assert np.all(np.abs(got - want) <= _logit_tol(want))
+    _no_device_errors(cbmoe)

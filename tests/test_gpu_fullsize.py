@@ -70,12 +70,23 @@ def test_config2_skewed_batch(setup, path):
 
 
 def test_config3_prefill_rows(setup):
+    """Config 3 on the grouped path, checked on 272 token rows: for every expert, the first and the last token routed
+    to it (so every expert's first and last 128-row block is covered), the first and last 8 tokens, and spread ones
+    up to 272."""
     cbmoe, L, p, _ = setup
     rng = np.random.default_rng(4096)
     x = gen.activations(rng, 4096, H)
     idx, w = gen.routing(rng, 4096, E, K)
     got = _run(cbmoe, p, x, idx, w, "grouped")
-    rows = np.concatenate([np.arange(8), np.sort(rng.choice(np.arange(8, 4096), 24, replace=False))])
+    ends = []
+    for e in range(E):
+        toks = np.nonzero((idx == e).any(axis=1))[0]
+        if toks.size:
+            ends += [toks[0], toks[-1]]
+    rows = np.unique(np.concatenate([np.arange(8), np.arange(4088, 4096), np.array(ends, np.int64)]))
+    rest = np.setdiff1d(np.arange(4096), rows)
+    rows = np.union1d(rows, rng.choice(rest, 272 - rows.size, replace=False))
+    assert rows.size == 272, rows.size
     want = _want(L, x[rows], idx[rows], w[rows])
     assert moe.max_rel_err(got[rows], want) < TOL
     assert np.isfinite(got).all()

@@ -102,3 +102,22 @@ def test_ragged_composition_reference_fixture(cbmoe):
     y = cbmoe.ResidentFetch(path="grouped").apply(p, t_bf16(x), torch.from_numpy(f["idx"]).cuda(),
                                                    torch.from_numpy(f["w"]).cuda(), 0, float(f["limit"]))
     assert moe.max_rel_err(y.cpu().numpy(), f["y"]) < LAYER_TOL
+
+
+@pytest.mark.parametrize("axis", [1, 0])
+@pytest.mark.parametrize("K,rows", [(5120, 12288), (12288, 5120)])
+def test_w8_linear_config3_projections_full_size(cbmoe, axis, K, rows):
+    """The config-3 dense projections at full size: QKV [5120 -> 96 x 128 = 12288] and O [12288 -> 5120] with 4096
+    tokens through the tcgen05 path, per-output-channel and per-input-row scales; a sample of 96 token rows (the
+    first, the last and spread ones) against quant8's dequant + fp64 product."""
+    T = 4096
+    rng = np.random.default_rng(K + axis)
+    q, s = gen.q8_leaf(rng, K, rows, axis)
+    x = gen.activations(rng, T, K)
+    qk = cbmoe.ops.pack_w8(torch.from_numpy(q).cuda())
+    y = cbmoe.ops.w8_linear(qk, torch.from_numpy(s.reshape(-1)).cuda(), axis, rows, K, t_bf16(x)).cpu().numpy()
+    sample = np.unique(np.concatenate([np.arange(16), np.arange(T - 16, T), rng.choice(T, 64, replace=False)]))
+    want = q8.matmul(x[sample].astype(np.float32), q, s)
+    assert moe.max_rel_err(y[sample], want) < MATVEC_TOL
+    assert np.isfinite(y).all()
+    assert cbmoe.device_errors(clear=True) == 0

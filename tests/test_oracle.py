@@ -133,3 +133,17 @@ def test_c_oracle_matches_numpy_oracle():
     assert moe.max_rel_err(got, want) < 1e-5
     y = cpu.cb3_matvec(L["down"][0][1], L["down"][1][1], x[:, :I] if False else rng.standard_normal((2, I)).astype(np.float32))
     assert y.shape == (2, H)
+
+
+def test_logits_colscale_matches_reference_fixture():
+    """oracle q8.logits_colscale against the reference's own `Engine._logits_local` with int8 columns (executed on the
+    NumPy stand-in by tests/golden/make_golden.py): bf16(f32(h @ q) * s). The reference sums in float32 and the
+    oracle in float64, so the bf16 logits agree to within one bf16 unit in the last place."""
+    import ml_dtypes
+    f = np.load(os.path.join(os.path.dirname(__file__), "golden", "logits_q8.npz"))
+    h = f["h"].view(ml_dtypes.bfloat16)
+    got = q8.logits_colscale(h, f["q"], f["s"]).astype(np.float32)
+    want = f["z"].view(ml_dtypes.bfloat16).astype(np.float32)
+    tol = np.abs(want) * 2.0 ** -7 + np.abs(want).max(axis=-1, keepdims=True) * 2.0 ** -12
+    assert np.all(np.abs(got - want) <= tol)
+    assert np.mean(got == want) > 0.95
