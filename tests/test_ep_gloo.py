@@ -30,17 +30,24 @@ def _all_to_all(send, nranks, cap):
     return torch.cat([b[rank * cap:(rank + 1) * cap] for b in bufs]).numpy()
 
 
-def _worker(rank, nranks, port, cap, result_q):
+def _worker(rank, nranks, port, cap, result_q, counts=None):
+    """`counts`: tokens per rank (default: 12 split evenly); `cap` None = the capacity cbmoe.ep.agree_capacity
+    agrees on (the largest N_local * k over the ranks), which is what the library's layer call uses."""
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=nranks)
     try:
         rng = np.random.default_rng(0)                       # same tables and tokens on every rank
         L = gen.moe_layer(rng, E, H, I)
-        N_total = 12
+        counts = counts or [12 // nranks] * nranks
+        N_total = sum(counts)
         x = gen.activations(rng, N_total, H).astype(np.float32)
         idx, w = gen.routing(rng, N_total, E, K_TOP)
-        per = N_total // nranks
-        xs, ids, ws = x[rank * per:(rank + 1) * per], idx[rank * per:(rank + 1) * per], w[rank * per:(rank + 1) * per]
+        per, a0 = counts[rank], sum(counts[:rank])
+        xs, ids, ws = x[a0:a0 + per], idx[a0:a0 + per], w[a0:a0 + per]
+        if cap is None:
+            from cbmoe.ep import agree_capacity
+            cap = agree_capacity(per, K_TOP)
+            assert cap == max(counts) * K_TOP, (cap, counts)
         send_eid, slot_pos, dropped = ep.route(ids, E, nranks, cap)
         send_x = np.zeros((nranks * cap, H), np.float32)
         for s, pos in enumerate(slot_pos):
@@ -101,5 +108,22 @@ def test_ep_protocol_four_ranks():
         assert p.exitcode == 0, "rank failed"
     res = [q.get(timeout=10) for _ in procs]
     assert sorted(r for r, _, _ in res) == [0, 1, 2, 3]
+    for rank, err, dropped in res:
+        assert dropped == 0 and err < 1e-6, (rank, err, dropped)
+
+
+def test_ep_unequal_token_counts_agree_on_capacity():
+    """Ranks holding different token counts (3 and 7): the default capacity is agreed by an all-reduce MAX
+    (cbmoe.ep.agree_capacity), so both ranks address each other's receive rows alike and nothing drops."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, None, q, [3, 7])) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+        assert p.exitcode == 0, "rank failed"
+    res = [q.get(timeout=10) for _ in procs]
     for rank, err, dropped in res:
         assert dropped == 0 and err < 1e-6, (rank, err, dropped)
