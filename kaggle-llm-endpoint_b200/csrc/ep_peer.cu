@@ -34,15 +34,18 @@ struct PeerPtrs {
 
 struct EpPeer {
   int nranks = 0, rank = 0, cap = 0, H = 0;
-  size_t off_x = 0, off_meta = 0, off_y = 0, off_fx = 0, off_fy = 0, off_ctr = 0, bytes = 0;
+  size_t off_x = 0, off_meta = 0, off_y = 0, off_fx = 0, off_fy = 0, off_ctr = 0, off_poison = 0, bytes = 0;
   uint8_t* own = nullptr;
   PeerPtrs peers{};
   uint32_t seq = 0;
-  // Poison word in mapped pinned host memory: a wait kernel that gave up sets it; from then on the transport's
-  // kernels write nothing to peers and wait for nothing, and cbmoe_ep_layer returns CBMOE_ERR_DEVICE (it reads
-  // the host side without synchronizing) until the peer is destroyed and set up again.
+  // Poison: a wait kernel that gave up sets the device word (in this rank's own buffer, which the transport's
+  // kernels read: an L2 hit) and its mirror in mapped pinned host memory (written only then, never read by a
+  // kernel: a read of host memory from every thread would cross PCIe). From then on the transport's kernels write
+  // nothing to peers and wait for nothing, and cbmoe_ep_layer returns CBMOE_ERR_DEVICE (it reads the host mirror
+  // without synchronizing) until the peer is destroyed and set up again.
   volatile int* poison_host = nullptr;
-  int* poison_dev = nullptr;
+  int* poison_mirror = nullptr;   // device address of poison_host
+  int* poison_dev = nullptr;      // own + off_poison
 };
 
 namespace {
@@ -128,7 +131,7 @@ __global__ void ep_return_kernel(const T* __restrict__ y_sorted, const int32_t* 
 
 // One CTA: wait until every source's flag reached seq (bounded; on expiry CBMOE_DEVERR_TIMEOUT, the poison word
 // is set and the kernel returns). A poisoned transport waits for nothing.
-__global__ void ep_wait_kernel(const uint32_t* flags, int nranks, uint32_t seq, int* poison) {
+__global__ void ep_wait_kernel(const uint32_t* flags, int nranks, uint32_t seq, int* poison, int* poison_mirror) {
   const int t = threadIdx.x;
   if (t < nranks && !poisoned(poison)) {
     const unsigned long long t0 = globaltimer_ns();
@@ -136,6 +139,7 @@ __global__ void ep_wait_kernel(const uint32_t* flags, int nranks, uint32_t seq, 
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
         atomicOr(&g_device_errors, CBMOE_DEVERR_TIMEOUT);
         *reinterpret_cast<volatile int*>(poison) = 1;
+        *reinterpret_cast<volatile int*>(poison_mirror) = 1;
         __threadfence_system();
         break;
       }
@@ -166,7 +170,7 @@ int ep_peer_dispatch(EpPeer* pe, const uint16_t* x, int H, const int32_t* slot_p
       reinterpret_cast<const uint4*>(x), H16, slot_pos, S, k, send_meta, pe->nranks, pe->rank, pe->cap, pe->peers,
       pe->off_x, pe->off_meta, pe->off_fx, ctr, pe->seq, pe->poison_dev);
   ep_wait_kernel<<<1, 64, 0, stream>>>(reinterpret_cast<const uint32_t*>(pe->own + pe->off_fx), pe->nranks, pe->seq,
-                                       pe->poison_dev);
+                                       pe->poison_dev, pe->poison_mirror);
   prof_end(kProfExchange, stream);
   prof_add_launches(2);
   CBMOE_CUDA_TRY(cudaGetLastError());
@@ -187,7 +191,7 @@ int ep_peer_return(EpPeer* pe, const void* y_sorted, bool bf16, const int32_t* r
         static_cast<const float*>(y_sorted), row_slot, recv_meta, R, H, pe->cap, pe->nranks, pe->rank, pe->peers,
         pe->off_y, pe->off_fy, ctr, pe->seq, pe->poison_dev);
   ep_wait_kernel<<<1, 64, 0, stream>>>(reinterpret_cast<const uint32_t*>(pe->own + pe->off_fy), pe->nranks, pe->seq,
-                                       pe->poison_dev);
+                                       pe->poison_dev, pe->poison_mirror);
   prof_end(kProfExchange, stream);
   prof_add_launches(2);
   CBMOE_CUDA_TRY(cudaGetLastError());
@@ -233,7 +237,8 @@ extern "C" int cbmoe_ep_peer_init(void* comm_v, int nranks, int rank, int H, int
   pe->off_fx = pe->off_y + lyr::align_up(rows * H * 4);
   pe->off_fy = pe->off_fx + 256;
   pe->off_ctr = pe->off_fy + 256;
-  pe->bytes = pe->off_ctr + 256;
+  pe->off_poison = pe->off_ctr + 256;
+  pe->bytes = pe->off_poison + 256;
   int rc = CBMOE_OK;
   uint8_t* records_dev = nullptr;
   std::vector<PeerRecord> records(nranks);
@@ -254,9 +259,10 @@ extern "C" int cbmoe_ep_peer_init(void* comm_v, int nranks, int rank, int H, int
   if (poison) {
     pe->poison_host = static_cast<volatile int*>(poison);
     *pe->poison_host = 0;
-    if (!rc && cudaHostGetDevicePointer(reinterpret_cast<void**>(&pe->poison_dev), poison, 0) != cudaSuccess)
+    if (!rc && cudaHostGetDevicePointer(reinterpret_cast<void**>(&pe->poison_mirror), poison, 0) != cudaSuccess)
       rc = CBMOE_ERR_CUDA;
   }
+  if (pe->own) pe->poison_dev = reinterpret_cast<int*>(pe->own + pe->off_poison);   // zeroed with the buffer
   // Every rank takes part in the all-gather even when its own set-up failed (the others would wait for it); a
   // failed rank contributes a zeroed record, which the others reject as a mismatch.
   if (records_dev && ncclAllGather(records_dev + (size_t)rank * sizeof(PeerRecord), records_dev,
