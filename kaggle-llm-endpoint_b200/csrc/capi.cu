@@ -61,9 +61,16 @@ int decode_tail_items(long long items) {
 // rows, and the down kernel takes the same passes in tiles of 2 slots (2 * nt tiles).
 int cb8_nt_routed(long long S, int E) { return S <= 2LL * E ? 1 : 2; }
 
+// The CB8 kernels up to 4 slots per expert on average, the bf16 ones above: per token tile the CB8 kernels do 2
+// (gate/up) or 8 (down) int8 MMAs per 32 inputs where the bf16 ones do 2 and 4 per 16 for twice the tokens, so the
+// table lookups they save stop paying once passes fill several tiles (measured on one B200, 160 experts at 12.8
+// slots each, 16-token passes: CB8 gate/up 589 us, down 682 us; the grouped GEMMs 506 and 362 us).
+bool use_cb8(long long S, int E, int cb8) { return cb8 && S <= 4LL * E; }
+
 DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k, long long slots_hint, int cb8) {
   DecodeWorkspace w;
   const long long S_real = slots_hint >= 0 ? (slots_hint < N ? slots_hint : N) : (long long)N * k;
+  cb8 = use_cb8(S_real, E, cb8) ? 1 : 0;
   w.cb8 = cb8;
   if (cb8) {
     w.nt = cb8_nt_routed(S_real, E);

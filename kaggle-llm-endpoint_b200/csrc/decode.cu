@@ -847,7 +847,7 @@ int launch_cb8_nt(const DecodeParams& p, int nt, int kind, cudaStream_t stream) 
   if constexpr (HILO != 0) {   // slot tiles of 2: 2 or 4 tiles (passes of up to 4 or 8 slots)
     if (nt <= 2) return launch_decode_t<FMT, NMAT, 2, EPI, HILO, NS>(p, kind, stream);
     return launch_decode_t<FMT, NMAT, 4, EPI, HILO, NS>(p, kind, stream);
-  } else {
+  } else {                     // token tiles of 4: 1 or 2 tiles (passes of up to 4 or 8 tokens)
     if (nt <= 1) return launch_decode_t<FMT, NMAT, 1, EPI, HILO, NS>(p, kind, stream);
     return launch_decode_t<FMT, NMAT, 2, EPI, HILO, NS>(p, kind, stream);
   }

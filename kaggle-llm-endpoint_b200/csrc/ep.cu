@@ -113,9 +113,9 @@ EpWorkspace ep_workspace(int E_loc, int H, int I, int N_local, int k, int nranks
   w.sub_recv = w.sub_local + align_up(w.Wl.total);
   // The receive buffer holds up to R rows, but a rank expects about its own slot count (N_local * k) of real
   // ones: AUTO chooses the kernels by that. From 8 rows per local expert on, the tensor-core GEMMs, except where
-  // the rank holds 32 or more experts with at most 16 rows each: there the decode kernels (16-token passes) are
-  // faster (measured on one B200 at 12.8 rows per expert, routed part: 40 experts 253 us decode vs 279 us
-  // grouped, 80 experts 436 vs 489 us; 20 experts 167 vs 159 us).
+  // the rank holds 32 or more experts with at most 16 rows each: there the decode kernels (the bf16 ones at that
+  // load: 16-token passes) are faster (measured on one B200 at 12.8 rows per expert, routed part: 40 experts 253 us
+  // decode vs 279 us grouped, 80 experts 436 vs 489 us; 20 experts 167 vs 159 us).
   const long long expect = (long long)N_local * k;
   const bool grouped_ok = H % kGrpTileM == 0 && I % kGrpTileM == 0;
   if (path == CBMOE_PATH_GROUPED && grouped_ok) {

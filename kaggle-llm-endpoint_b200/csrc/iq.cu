@@ -20,11 +20,15 @@ template <int T>
 __global__ void iq_dequant_kernel(const uint8_t* __restrict__ blocks, long long n_blocks,
                                   const float* __restrict__ table, float* __restrict__ out) {
   constexpr int BB = IqFmt<T>::kBytes;
+  constexpr int TAB = IqFmt<T>::kEntries * IqFmt<T>::kWidth;   // 0: no lookup table (K-quants)
+  __shared__ __align__(16) float tab[TAB > 0 ? TAB : 4];         // grid rows 16-byte aligned for iq_lane8
+  for (int i = threadIdx.x; i < TAB; i += blockDim.x) tab[i] = table[i];
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   const long long warps = ((long long)gridDim.x * blockDim.x) >> 5;
   for (long long b = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; b < n_blocks; b += warps) {
     float v[8];
-    iq_lane8<T>(blocks + b * BB, lane, table, v);
+    iq_lane8<T>(blocks + b * BB, lane, tab, v);
     float4* o = reinterpret_cast<float4*>(out + b * 256 + 8 * lane);
     o[0] = make_float4(v[0], v[1], v[2], v[3]);
     o[1] = make_float4(v[4], v[5], v[6], v[7]);
@@ -47,13 +51,16 @@ int launch_iq(const void* blocks, long long n_blocks, const float* table, float*
 // The decode composition of resident.py:110-120 (`_apply_kernel`: gate/up -> swiglu_clamped -> down -> weighted sum
 // of the slots) over raw GGUF IQ tables, computing in fp32 as the reference's moe_matvec does
 // (pallas_moe.py:238-307: on-the-fly dequant, fp32 products and sums). Rows of the routing plan are grouped in
-// passes of up to kIqPassTokens slots of one expert; an item is (pass, weight row), one warp per item: each lane
-// dequantizes its 8 weights of every 256-weight block of the row once (iq_lane8, the table in shared memory) and
-// multiply-adds them into one fp32 partial per token of the pass; a warp sum gives the row's outputs.
+// passes of up to kIqPassTokens slots of one expert; an item is (pass, kIqRows consecutive weight rows), one warp
+// per item: for every 256-weight block, each lane loads its 8 inputs of every token of the pass once (registers),
+// then dequantizes its 8 weights of each of the item's rows (iq_lane8, the table in shared memory) and multiply-adds
+// them into one fp32 partial per (row, token); warp sums give the outputs. The rows of an item share the input
+// loads, and their dequant chains are independent (instruction-level parallelism).
 //   gate, up: x = the slots' token rows (bf16, through the plan's row -> token map) -> g, u fp32 [sorted row][I]
 //   h = swiglu_clamped(g, u) (elementwise, into g's buffer)
 //   down:     x = h (fp32 sorted rows) -> y fp32 [sorted row][H]; combine_kernel sums the slots.
 constexpr int kIqPassTokens = 8;
+constexpr int kIqRows = 4;   // weight rows per item (rows are multiples of 256)
 
 struct IqMatParams {
   const uint8_t* w;          // raw blocks [E][rows][K / 256][block bytes]
@@ -78,58 +85,83 @@ __device__ __forceinline__ void bf16x8(const uint4& q, float (&f)[8]) {
   }
 }
 
-template <int T, int H_IN>
-__global__ void __launch_bounds__(256) iq_matvec_kernel(const IqMatParams p) {
+// PT: tokens held in registers at a time (2 for small passes: more warps per SM; 8 for full ones); a pass of more
+// tokens is walked in chunks of PT, each chunk dequantizing the weights again.
+template <int T, int H_IN, int PT>
+__global__ void __launch_bounds__(256, PT <= 2 ? 3 : 1) iq_matvec_kernel(const IqMatParams p) {
   constexpr int BB = IqFmt<T>::kBytes;
   constexpr int TAB = IqFmt<T>::kEntries * IqFmt<T>::kWidth;   // 0: no lookup table (K-quants)
-  __shared__ float tab[TAB > 0 ? TAB : 1];
+  __shared__ __align__(16) float tab[TAB > 0 ? TAB : 4];
   for (int i = threadIdx.x; i < TAB; i += blockDim.x) tab[i] = p.table[i];
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int nblk = p.K / 256;
-  const long long items = (long long)(*p.n_pass) * p.rows;
+  const int groups = p.rows / kIqRows;
+  const long long items = (long long)(*p.n_pass) * groups;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
   for (long long it = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += warps) {
-    const int pass = (int)(it / p.rows), r = (int)(it % p.rows);
-    const int e = p.pass_expert[pass], row0 = p.pass_row0[pass];
-    const int cnt = min(p.pass_cnt[pass], kIqPassTokens);
-    if (e < 0 || e >= p.E || cnt <= 0) continue;
-    const uint8_t* wrow = p.w + ((size_t)e * p.rows + r) * nblk * BB;
-    int tok[kIqPassTokens];
+    const int pass = (int)(it / groups), r0 = (int)(it % groups) * kIqRows;
+    const int e = p.pass_expert[pass], row0_pass = p.pass_row0[pass];
+    const int cnt_pass = min(p.pass_cnt[pass], kIqPassTokens);
+    if (e < 0 || e >= p.E || cnt_pass <= 0) continue;
+    const uint8_t* wrow = p.w + ((size_t)e * p.rows + r0) * nblk * BB;
+    const size_t row_stride = (size_t)nblk * BB;
+    for (int c0 = 0; c0 < cnt_pass; c0 += PT) {
+      const int row0 = row0_pass + c0, cnt = min(PT, cnt_pass - c0);
+      const uint16_t* xr[PT];
+      const float* hr[PT];
 #pragma unroll
-    for (int t = 0; t < kIqPassTokens; ++t) tok[t] = (!H_IN && t < cnt) ? p.tok_row[row0 + t] : 0;
-    float acc[kIqPassTokens];
-#pragma unroll
-    for (int t = 0; t < kIqPassTokens; ++t) acc[t] = 0.f;
-    for (int b = 0; b < nblk; ++b) {
-      float v[8];
-      iq_lane8<T>(wrow + (size_t)b * BB, lane, tab, v);
-      const int k0 = b * 256 + 8 * lane;
-#pragma unroll
-      for (int t = 0; t < kIqPassTokens; ++t) {
-        if (t >= cnt) break;
-        float xv[8];
-        if constexpr (H_IN) {
-          const float* hp = p.h + (size_t)(row0 + t) * p.K + k0;
-          const float4 h0 = *reinterpret_cast<const float4*>(hp), h1 = *reinterpret_cast<const float4*>(hp + 4);
-          xv[0] = h0.x; xv[1] = h0.y; xv[2] = h0.z; xv[3] = h0.w;
-          xv[4] = h1.x; xv[5] = h1.y; xv[6] = h1.z; xv[7] = h1.w;
-        } else {
-          bf16x8(*reinterpret_cast<const uint4*>(p.x + (size_t)tok[t] * p.K + k0), xv);
-        }
-        float a = acc[t];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) a = fmaf(v[j], xv[j], a);
-        acc[t] = a;
+      for (int t = 0; t < PT; ++t) {
+        const int tt = t < cnt ? t : 0;
+        xr[t] = H_IN ? nullptr : p.x + (size_t)p.tok_row[row0 + tt] * p.K + 8 * lane;
+        hr[t] = H_IN ? p.h + (size_t)(row0 + tt) * p.K + 8 * lane : nullptr;
       }
-    }
+      float acc[kIqRows][PT];
 #pragma unroll
-    for (int t = 0; t < kIqPassTokens; ++t) {
-      if (t >= cnt) break;
-      float a = acc[t];
+      for (int r = 0; r < kIqRows; ++r)
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-      if (lane == 0) p.out[(size_t)(row0 + t) * p.rows + r] = a;
+        for (int t = 0; t < PT; ++t) acc[r][t] = 0.f;
+      for (int b = 0; b < nblk; ++b) {
+        float xv[PT][8];
+#pragma unroll
+        for (int t = 0; t < PT; ++t) {
+          if (t < cnt) {
+            if constexpr (H_IN) {
+              const float4 h0 = __ldg(reinterpret_cast<const float4*>(hr[t] + b * 256));
+              const float4 h1 = __ldg(reinterpret_cast<const float4*>(hr[t] + b * 256) + 1);
+              xv[t][0] = h0.x; xv[t][1] = h0.y; xv[t][2] = h0.z; xv[t][3] = h0.w;
+              xv[t][4] = h1.x; xv[t][5] = h1.y; xv[t][6] = h1.z; xv[t][7] = h1.w;
+            } else {
+              bf16x8(__ldg(reinterpret_cast<const uint4*>(xr[t] + b * 256)), xv[t]);
+            }
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < kIqRows; ++r) {
+          float v[8];
+          iq_lane8<T>(wrow + r * row_stride + (size_t)b * BB, lane, tab, v);
+#pragma unroll
+          for (int t = 0; t < PT; ++t) {
+            if (t < cnt) {
+              float a = acc[r][t];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) a = fmaf(v[j], xv[t][j], a);
+              acc[r][t] = a;
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < PT; ++t) {
+        if (t >= cnt) break;
+#pragma unroll
+        for (int r = 0; r < kIqRows; ++r) {
+          float a = acc[r][t];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+          if (lane == r) p.out[(size_t)(row0 + t) * p.rows + r0 + r] = a;
+        }
+      }
     }
   }
 }
@@ -140,20 +172,27 @@ __global__ void iq_swiglu_kernel(float* __restrict__ g, const float* __restrict_
     g[i] = swiglu_clamped(g[i], u[i], limit);
 }
 
+template <int H_IN, int PT>
+void launch_iq_matvec_pt(int type, const IqMatParams& p, int grid, cudaStream_t s) {
+  switch (type) {
+    case CBMOE_GGML_IQ2_S: iq_matvec_kernel<CBMOE_GGML_IQ2_S, H_IN, PT><<<grid, 256, 0, s>>>(p); break;
+    case CBMOE_GGML_IQ3_S: iq_matvec_kernel<CBMOE_GGML_IQ3_S, H_IN, PT><<<grid, 256, 0, s>>>(p); break;
+    case CBMOE_GGML_IQ4_XS: iq_matvec_kernel<CBMOE_GGML_IQ4_XS, H_IN, PT><<<grid, 256, 0, s>>>(p); break;
+    case CBMOE_GGML_Q2_K: iq_matvec_kernel<CBMOE_GGML_Q2_K, H_IN, PT><<<grid, 256, 0, s>>>(p); break;
+    default: iq_matvec_kernel<CBMOE_GGML_Q3_K, H_IN, PT><<<grid, 256, 0, s>>>(p); break;
+  }
+}
+
+// small: the passes average at most 2 tokens (the 2-token register variant, 3 CTAs per SM)
 template <int H_IN>
-int launch_iq_matvec(int type, const IqMatParams& p, long long max_items, int kind, cudaStream_t s) {
-  long long grid = (max_items + 7) / 8;
-  const long long cap = (long long)num_sms() * 8;
+int launch_iq_matvec(int type, const IqMatParams& p, long long max_items, bool small, int kind, cudaStream_t s) {
+  long long grid = (max_items / kIqRows + 7) / 8;
+  const long long cap = (long long)num_sms() * (small ? 3 : 1);
   if (grid > cap) grid = cap;
   if (grid < 1) grid = 1;
   prof_begin(kind, s);
-  switch (type) {
-    case CBMOE_GGML_IQ2_S: iq_matvec_kernel<CBMOE_GGML_IQ2_S, H_IN><<<(int)grid, 256, 0, s>>>(p); break;
-    case CBMOE_GGML_IQ3_S: iq_matvec_kernel<CBMOE_GGML_IQ3_S, H_IN><<<(int)grid, 256, 0, s>>>(p); break;
-    case CBMOE_GGML_IQ4_XS: iq_matvec_kernel<CBMOE_GGML_IQ4_XS, H_IN><<<(int)grid, 256, 0, s>>>(p); break;
-    case CBMOE_GGML_Q2_K: iq_matvec_kernel<CBMOE_GGML_Q2_K, H_IN><<<(int)grid, 256, 0, s>>>(p); break;
-    default: iq_matvec_kernel<CBMOE_GGML_Q3_K, H_IN><<<(int)grid, 256, 0, s>>>(p); break;
-  }
+  if (small) launch_iq_matvec_pt<H_IN, 2>(type, p, (int)grid, s);
+  else launch_iq_matvec_pt<H_IN, kIqPassTokens>(type, p, (int)grid, s);
   prof_end(kind, s);
   CBMOE_CUDA_TRY(cudaGetLastError());
   return CBMOE_OK;
@@ -227,15 +266,16 @@ extern "C" int cbmoe_iq_experts_apply(const cbmoe_iq_experts* ex, const uint16_t
   p.x = x;
   p.tok_row = plan + W.L.off[7];
   const long long items_gu = (long long)W.P * ex->I, items_dn = (long long)W.P * ex->H;
+  const bool small = (long long)N * k <= 2LL * ex->E;
   p.w = static_cast<const uint8_t*>(ex->gate);
   p.table = ex->gate_table;
   p.out = g;
-  rc = launch_iq_matvec<0>(ex->gate_type, p, items_gu, kProfIqGateUp, stream);
+  rc = launch_iq_matvec<0>(ex->gate_type, p, items_gu, small, kProfIqGateUp, stream);
   if (rc) return rc;
   p.w = static_cast<const uint8_t*>(ex->up);
   p.table = ex->up_table;
   p.out = u;
-  rc = launch_iq_matvec<0>(ex->up_type, p, items_gu, kProfIqGateUp, stream);
+  rc = launch_iq_matvec<0>(ex->up_type, p, items_gu, small, kProfIqGateUp, stream);
   if (rc) return rc;
   {
     const long long n = (long long)W.Rp * ex->I;
@@ -255,7 +295,7 @@ extern "C" int cbmoe_iq_experts_apply(const cbmoe_iq_experts* ex, const uint16_t
   d.tok_row = nullptr;
   d.h = g;
   d.out = ys;
-  rc = launch_iq_matvec<1>(ex->down_type, d, items_dn, kProfIqDown, stream);
+  rc = launch_iq_matvec<1>(ex->down_type, d, items_dn, small, kProfIqDown, stream);
   if (rc) return rc;
   return launch_combine(ys, plan + W.L.off[9], w, N, k, ex->H, nullptr, y, nullptr, stream);
 }

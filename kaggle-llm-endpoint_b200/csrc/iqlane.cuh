@@ -69,6 +69,24 @@ __host__ __device__ __forceinline__ float with_sign(float v, unsigned sign_byte,
   return ((sign_byte >> k) & 1u) ? -v : v;
 }
 
+// W consecutive table values (a grid row: 16-byte aligned in the kernels' shared-memory copy, so one or two
+// 16-byte loads there).
+template <int W>
+__host__ __device__ __forceinline__ void grid_row(const float* row, float (&out)[W]) {
+#ifdef __CUDA_ARCH__
+#pragma unroll
+  for (int i = 0; i < W / 4; ++i) {
+    const float4 q = reinterpret_cast<const float4*>(row)[i];
+    out[4 * i] = q.x;
+    out[4 * i + 1] = q.y;
+    out[4 * i + 2] = q.z;
+    out[4 * i + 3] = q.w;
+  }
+#else
+  for (int i = 0; i < W; ++i) out[i] = row[i];
+#endif
+}
+
 template <int T>
 __host__ __device__ __forceinline__ void iq_lane8(const uint8_t* __restrict__ blk, int lane, const float* table,
                                                   float (&v)[8]) {
@@ -79,8 +97,10 @@ __host__ __device__ __forceinline__ void iq_lane8(const uint8_t* __restrict__ bl
     const int s = (blk[74 + g / 4] >> (4 * ((g / 2) % 2))) & 15;
     const unsigned sg = blk[34 + g];
     const float db = iq_mul(iq_mul(d, 0.5f + (float)s), 0.25f);
+    float gr[8];
+    grid_row<8>(table + idx * 8, gr);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = with_sign(iq_mul(db, table[idx * 8 + k]), sg, k);
+    for (int k = 0; k < 8; ++k) v[k] = with_sign(iq_mul(db, gr[k]), sg, k);
   } else if constexpr (T == CBMOE_GGML_IQ3_S) {
     const float d = f16_at(blk);
     const int m = lane / 4;   // 32-weight scale group
@@ -91,8 +111,10 @@ __host__ __device__ __forceinline__ void iq_lane8(const uint8_t* __restrict__ bl
     for (int h = 0; h < 2; ++h) {
       const int G = 2 * lane + h;
       const int idx = blk[2 + G] | (((blk[66 + G / 8] >> (G % 8)) & 1) << 8);
+      float gr[4];
+      grid_row<4>(table + idx * 4, gr);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) v[4 * h + q] = with_sign(iq_mul(db, table[idx * 4 + q]), sg, 4 * h + q);
+      for (int q = 0; q < 4; ++q) v[4 * h + q] = with_sign(iq_mul(db, gr[q]), sg, 4 * h + q);
     }
   } else if constexpr (T == CBMOE_GGML_IQ4_XS) {
     const float d = f16_at(blk);
