@@ -160,8 +160,8 @@ int grid_for(long long work) {
 
 size_t ep_peer_capacity(const EpPeer* pe) { return pe ? (size_t)pe->cap : 0; }
 
-int ep_peer_dispatch(EpPeer* pe, const uint16_t* x, int H, const int32_t* slot_pos, int S, int k,
-                     const int32_t* send_meta, cudaStream_t stream) {
+int ep_peer_dispatch_send(EpPeer* pe, const uint16_t* x, int H, const int32_t* slot_pos, int S, int k,
+                          const int32_t* send_meta, cudaStream_t stream) {
   ++pe->seq;
   const int H16 = H / 8;
   uint32_t* ctr = reinterpret_cast<uint32_t*>(pe->own + pe->off_ctr);
@@ -169,10 +169,16 @@ int ep_peer_dispatch(EpPeer* pe, const uint16_t* x, int H, const int32_t* slot_p
   ep_dispatch_kernel<<<grid_for((long long)S * H16 + (long long)pe->nranks * pe->cap), 256, 0, stream>>>(
       reinterpret_cast<const uint4*>(x), H16, slot_pos, S, k, send_meta, pe->nranks, pe->rank, pe->cap, pe->peers,
       pe->off_x, pe->off_meta, pe->off_fx, ctr, pe->seq, pe->poison_dev);
+  prof_add_launches(1);
+  CBMOE_CUDA_TRY(cudaGetLastError());
+  return CBMOE_OK;
+}
+
+int ep_peer_dispatch_wait(EpPeer* pe, cudaStream_t stream) {
   ep_wait_kernel<<<1, 64, 0, stream>>>(reinterpret_cast<const uint32_t*>(pe->own + pe->off_fx), pe->nranks, pe->seq,
                                        pe->poison_dev, pe->poison_mirror);
   prof_end(kProfExchange, stream);
-  prof_add_launches(2);
+  prof_add_launches(1);
   CBMOE_CUDA_TRY(cudaGetLastError());
   return CBMOE_OK;
 }

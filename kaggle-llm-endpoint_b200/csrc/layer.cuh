@@ -80,8 +80,11 @@ int routed_grouped(const cbmoe_experts* ex, const uint16_t* x, int N, const int3
 struct EpPeer;
 bool ep_peer_matches(const EpPeer* pe, int nranks, int rank, int H, int cap);
 bool ep_peer_poisoned(const EpPeer* pe);
-int ep_peer_dispatch(EpPeer* pe, const uint16_t* x, int H, const int32_t* slot_pos, int S, int k,
-                     const int32_t* send_meta, cudaStream_t stream);
+// Dispatch in two launches: the rows into the peers' memory (send), then the wait for every peer's rows (wait);
+// the caller may queue independent work on other streams between the two.
+int ep_peer_dispatch_send(EpPeer* pe, const uint16_t* x, int H, const int32_t* slot_pos, int S, int k,
+                          const int32_t* send_meta, cudaStream_t stream);
+int ep_peer_dispatch_wait(EpPeer* pe, cudaStream_t stream);
 int ep_peer_return(EpPeer* pe, const void* y_sorted, bool bf16, const int32_t* row_slot, const int32_t* recv_meta,
                    int R, int H, cudaStream_t stream);
 uint16_t* ep_peer_in_x(EpPeer* pe);
