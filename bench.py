@@ -79,17 +79,20 @@ def config_block(n_gpus, transport=None):
 
 # ------------------------------------------------------------------------------------------------ clocks
 class ClockSampler:
-    """NVML polling thread: SM clock and throttle reasons while the timed region runs. Under torchrun only rank 0
-    samples (its own GPU), every 10 ms: NVML queries from every rank at a high rate slowed the timed multi-GPU steps
-    (8 ranks: 0.41 ms per step with them against 0.22 ms in the same run's unsampled end-to-end loop)."""
+    """NVML polling thread: SM clock and throttle reasons while the timed region runs, every 2 ms. NVML is
+    initialized, and the first query made, by start(), which callers run before the barrier that opens a timed
+    region: under torchrun the ranks wait for each other inside the region, so a rank still setting up NVML after
+    the barrier is timed by all the others (measured at 2 GPUs: 0.43-1.77 ms per step with rank 0 alone setting up
+    after the barrier, 0.20 ms with no sampler). Every rank samples its own GPU, so whatever the polling costs is
+    the same on every rank; rank 0 reports its own."""
 
-    def __init__(self, index, period_s=0.01, active=True):
+    def __init__(self, index, period_s=0.002, active=True):
         self.index, self.period, self.active = index, period_s, active
         self.samples, self.stop_ev, self.th = [], threading.Event(), None
         self.ok = False
 
-    def __enter__(self):
-        if not self.active:
+    def start(self):
+        if not self.active or self.th is not None or self.ok:
             return self
         try:
             import pynvml as nv
@@ -100,18 +103,23 @@ class ClockSampler:
         except Exception:
             return self
 
+        def sample():
+            try:
+                self.samples.append((self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM),
+                                     self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)))
+            except Exception:
+                pass
+
         def run():
-            nv = self.nv
-            while not self.stop_ev.is_set():
-                try:
-                    self.samples.append((nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM),
-                                         nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)))
-                except Exception:
-                    pass
-                time.sleep(self.period)
+            while not self.stop_ev.wait(self.period):
+                sample()
+        sample()   # the first query here, before the caller's barrier
         self.th = threading.Thread(target=run, daemon=True)
         self.th.start()
         return self
+
+    def __enter__(self):
+        return self.start()
 
     def __exit__(self, *a):
         self.stop_ev.set()
@@ -377,10 +385,11 @@ def run_ours(args):
     # ---- value: device-resident inputs, exactly K steps between events
     for s in range(args.warmup):
         step(s)
+    sampler = ClockSampler(local).start()
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     l0 = launch_count()
-    with ClockSampler(local, active=(rank == 0)) as clocks:
+    with sampler as clocks:
         ev0.record()
         for s in range(args.steps):
             step(args.warmup + s)
@@ -762,10 +771,11 @@ def config4_measure(args, world, rank, local, dev, group, with_e2e=True, with_ke
 
     for s in range(args.warmup):
         stack(*batches[s % n_batches])
+    sampler = ClockSampler(local).start()
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     l0 = launch_count()
-    with ClockSampler(local, active=(rank == 0)) as clocks:
+    with sampler as clocks:
         ev0.record()
         for s in range(args.steps):
             stack(*batches[(args.warmup + s) % n_batches])

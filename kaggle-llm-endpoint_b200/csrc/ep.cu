@@ -235,13 +235,13 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
 
   // shared expert of the local tokens on the side stream (gate/up, down -> ys), beside the dispatch and the local
   // experts; joined before the final combine. (Measured: joining it before the local experts, with the decode
-  // kernels on the whole GPU, is slower at 32-64 tokens per rank: those kernels outlast the dispatch.) With the
-  // peer transport it is forked right after this rank's rows are sent, on the whole GPU: the wait for the other
-  // ranks' rows leaves the SMs idle, and forked earlier it would delay the send every rank waits for.
+  // kernels on the whole GPU, is slower at 32-64 tokens per rank: those kernels outlast the dispatch; forking it
+  // after this rank's rows are sent, on the whole GPU, slowed the routed kernels that follow the wait: config 4 at
+  // 2 / 4 / 8 GPUs 128k / 173k / 205k tok/s against 135k / 200k / 209k with the 48-CTA side stream.)
   lyr::SideStream* side = nullptr;
   rc = lyr::side_stream(&side);
   if (rc) return rc;
-  if (N_local > 0 && !pe) {
+  if (N_local > 0) {
     rc = lyr::shared_side(sh, x, N_local, H, I, limit, wl, W.Wl, side, stream);
     if (rc) return rc;
   }
@@ -254,7 +254,6 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
   CBMOE_CUDA_TRY(cudaGetLastError());
   if (pe) {   // 2-3. rows straight into the destinations' memory
     rc = ep_peer_dispatch_send(pe, x, H, slot_pos, S, k, send_meta, stream);
-    if (!rc && N_local > 0) rc = lyr::shared_side(sh, x, N_local, H, I, limit, wl, W.Wl, side, stream, 0);
     if (!rc) rc = ep_peer_dispatch_wait(pe, stream);
     if (rc) goto join;
   }
