@@ -237,7 +237,9 @@ extern "C" int cbmoe_ep_layer(void* comm_v, int nranks, int rank, const cbmoe_ex
   // experts; joined before the final combine. (Measured: joining it before the local experts, with the decode
   // kernels on the whole GPU, is slower at 32-64 tokens per rank: those kernels outlast the dispatch; forking it
   // after this rank's rows are sent, on the whole GPU, slowed the routed kernels that follow the wait: config 4 at
-  // 2 / 4 / 8 GPUs 128k / 173k / 205k tok/s against 135k / 200k / 209k with the 48-CTA side stream.)
+  // 2 / 4 / 8 GPUs 128k / 173k / 205k tok/s against 135k / 200k / 209k with the 48-CTA side stream; running it on
+  // this stream between the send and the wait, on the whole GPU, measured slower again: config 4 at 2 / 8 GPUs
+  // 109k / 184k, the weak-scaling line 68k / 276k against 80k / 319k: its decode kernels outlast the wait.)
   lyr::SideStream* side = nullptr;
   rc = lyr::side_stream(&side);
   if (rc) return rc;
