@@ -46,7 +46,8 @@ int decode_nt_routed(int N, int k, int E) {
 // Workspace of the decode path:
 //   plan | x8 (N x H/256 x 512 B: the tokens as X8 rows, CB8 tables only) | x8 factors (N f32) |
 //   h (the SwiGLU output of the routed slots: Rp x 2I bf16 (hi, lo) for the bf16 kernels, Rp x I/256 x 1040 B H8
-//   rows for the CB8 ones) | y_sorted (Rp x H f32) | h_shared (N x 2I bf16) | y_shared (N x H f32) |
+//   rows for the CB8 ones) | y_sorted (Rp x H f32) | h_shared (N x 2I bf16, or N x I/256 x 1040 B H8 rows) |
+//   y_shared (N x H f32) | the shared expert's own X8 rows of x (N x H x 2 B) and factors (N f32) |
 //   scheduling words: routed [gate/up tickets, down tickets, gate/up arrival counters, down arrival counters]
 //                     (zeroed by the plan kernel), shared [the same] (zeroed by a memset on the side stream) |
 //   partial sums of the tail items' pieces of the routed gate/up, routed down, shared gate/up, shared down.
@@ -99,9 +100,12 @@ DecodeWorkspace decode_workspace(int E, int H, int I, int N, int k, long long sl
   w.x8s = w.x8 + align_up((size_t)N * H * 2);
   w.h = w.x8s + align_up((size_t)N * 4);
   w.y = w.h + align_up(h_bf16 > h_h8 ? h_bf16 : h_h8);
+  const size_t hs_bf16 = (size_t)N * 2 * I * 2, hs_h8 = (size_t)N * (I / kStageK) * kH8StageBytes;
   w.hs = w.y + align_up((size_t)w.Rp * H * 4);
-  w.ys = w.hs + align_up((size_t)N * 2 * I * 2);
-  w.done = w.ys + align_up((size_t)N * H * 4);
+  w.ys = w.hs + align_up(hs_bf16 > hs_h8 ? hs_bf16 : hs_h8);
+  w.xs8 = w.ys + align_up((size_t)N * H * 4);
+  w.xs8s = w.xs8 + align_up((size_t)N * H * 2);
+  w.done = w.xs8s + align_up((size_t)N * 4);
   w.part_gu = w.done + align_up((size_t)(w.n_zero_routed + w.n_zero_shared) * 4);
   w.part_dn = w.part_gu + align_up(decode_part_bytes(w.tail_gu, w.nt, 2));
   w.part_sgu = w.part_dn + align_up(decode_part_bytes(w.tail_dn, w.nt_dn, 1));
@@ -296,6 +300,55 @@ int shared_side(const cbmoe_shared* sh, const uint16_t* x, int N, int H, int I, 
     gd.E = 1;
     gd.out_f32 = reinterpret_cast<float*>(ws + W.ys);
     rc = grouped_w8_store_f32(gd, hs, N, ss);
+    if (rc) return rc;
+    CBMOE_CUDA_TRY(cudaEventRecord(side->join, side->s));
+    return CBMOE_OK;
+  }
+
+  if (W.cb8 && sh->scale_axis == 1 && N <= 8) {
+    // int8 MMA on the stored leaves (no dequant arithmetic, so the side stream takes fewer SM cycles from the routed
+    // kernels; config 1: CB8 gate+up 102 -> 92 us inside the layer): x split into its own X8 rows here, gate/up ->
+    // SwiGLU -> H8 rows, down -> ys. Whole items only. Up to one 8-token pass: its token tiles hold 4 tokens, so
+    // at 64 tokens it would stream the weights 8 times (measured slower there than the bf16 kernels' 32-token
+    // passes).
+    uint8_t* xs8 = ws + W.xs8;
+    float* xs8s = reinterpret_cast<float*>(ws + W.xs8s);
+    uint8_t* hs8 = ws + W.hs;
+    int rc = launch_split_x(x, N, H, xs8, xs8s, side->s);
+    if (rc) return rc;
+    const int nt = N <= 4 ? 1 : 2;
+    DecodeParams p = base_params();
+    p.wq = static_cast<const uint8_t*>(sh->gateup_q);
+    p.s0 = sh->gate_s;
+    p.s1 = sh->up_s;
+    p.scale_axis = 1;
+    p.rows = I;
+    p.K = H;
+    p.RB = I / kRowsPerBlock;
+    p.KS = H / kStageK;
+    p.b8 = xs8;
+    p.b8_scale = xs8s;
+    p.N = N;
+    p.limit = limit;
+    p.h8_out = hs8;
+    p.grid_cap = grid_cap;
+    p.sched = done_sh;
+    rc = decode_w8i_gateup(p, nt, side->s);
+    if (rc) return rc;
+    DecodeParams d = base_params();
+    d.wq = static_cast<const uint8_t*>(sh->down_q);
+    d.s0 = sh->down_s;
+    d.scale_axis = 1;
+    d.rows = H;
+    d.K = I;
+    d.RB = H / kRowsPerBlock;
+    d.KS = I / kStageK;
+    d.b8 = hs8;
+    d.N = N;
+    d.y_out = reinterpret_cast<float*>(ws + W.ys);
+    d.grid_cap = grid_cap;
+    d.sched = done_sh + 1;
+    rc = decode_w8i_down(d, 2 * nt, side->s);
     if (rc) return rc;
     CBMOE_CUDA_TRY(cudaEventRecord(side->join, side->s));
     return CBMOE_OK;

@@ -568,36 +568,46 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<FMT, NT, HIL
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
               if (!(n == 0 || n * SM::kTokPerTile < h.cnt)) continue;
-              mma_i8<false>(ci_hi[m][n], ah[0], bx[n].x, bx[n].y);
-              mma_i8<false>(ci_hi[m][n], ah[1], bx[n].z, bx[n].w);
+              if constexpr (HILO) {
+                // H8 rows: this chunk's exact products, times the factor of the chunk and of the digit column
+                int dh[4] = {0, 0, 0, 0};
+                mma_i8<false>(dh, ah[0], bx[n].x, bx[n].y);
+                mma_i8<false>(dh, ah[1], bx[n].z, bx[n].w);
+                const float F = *reinterpret_cast<const float*>(sb + (n * 2 + (t >> 1)) * SM::kBRow + 1024 + 4 * c);
+                const float f0 = (t & 1) ? F * 65536.f : F, f1 = f0 * 256.f;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[m][n][i] += (float)dh[i] * ((i & 1) ? f1 : f0);
+              } else {
+                mma_i8<false>(ci_hi[m][n], ah[0], bx[n].x, bx[n].y);
+                mma_i8<false>(ci_hi[m][n], ah[1], bx[n].z, bx[n].w);
+              }
             }
-            continue;
           } else {
             cb8_dequant_chunk<FMT == kFmtCB8 ? CBMOE_CB8_FMA_MODE : 0>(wd[m][3 * c], wd[m][3 * c + 1],
                                                                         wd[m][3 * c + 2], c8g[m], c8h[m], p.sel, ah,
                                                                         al);
-          }
 #pragma unroll
-          for (int n = 0; n < NT; ++n) {
-            if (!(n == 0 || n * SM::kTokPerTile < h.cnt)) continue;
-            if constexpr (HILO) {
-              // this chunk's exact products (T = 256 hi + lo), then times the factor of the chunk and of the part
-              // (digit p of the slot's h: 256^p)
-              int dh[4] = {0, 0, 0, 0}, dl[4] = {0, 0, 0, 0};
-              mma_i8<false>(dh, ah[0], bx[n].x, bx[n].y);
-              mma_i8<true>(dl, al[0], bx[n].x, bx[n].y);
-              mma_i8<false>(dh, ah[1], bx[n].z, bx[n].w);
-              mma_i8<true>(dl, al[1], bx[n].z, bx[n].w);
-              const float F = *reinterpret_cast<const float*>(sb + (n * 2 + (t >> 1)) * SM::kBRow + 1024 + 4 * c);
-              const float f0 = (t & 1) ? F * 65536.f : F, f1 = f0 * 256.f;
+            for (int n = 0; n < NT; ++n) {
+              if (!(n == 0 || n * SM::kTokPerTile < h.cnt)) continue;
+              if constexpr (HILO) {
+                // this chunk's exact products (T = 256 hi + lo), then times the factor of the chunk and of the part
+                // (digit p of the slot's h: 256^p)
+                int dh[4] = {0, 0, 0, 0}, dl[4] = {0, 0, 0, 0};
+                mma_i8<false>(dh, ah[0], bx[n].x, bx[n].y);
+                mma_i8<true>(dl, al[0], bx[n].x, bx[n].y);
+                mma_i8<false>(dh, ah[1], bx[n].z, bx[n].w);
+                mma_i8<true>(dl, al[1], bx[n].z, bx[n].w);
+                const float F = *reinterpret_cast<const float*>(sb + (n * 2 + (t >> 1)) * SM::kBRow + 1024 + 4 * c);
+                const float f0 = (t & 1) ? F * 65536.f : F, f1 = f0 * 256.f;
 #pragma unroll
-              for (int i = 0; i < 4; ++i)
-                acc[m][n][i] += (float)(dh[i] * 256 + dl[i]) * ((i & 1) ? f1 : f0);
-            } else {
-              mma_i8<false>(ci_hi[m][n], ah[0], bx[n].x, bx[n].y);
-              mma_i8<true>(ci_lo[m][n], al[0], bx[n].x, bx[n].y);
-              mma_i8<false>(ci_hi[m][n], ah[1], bx[n].z, bx[n].w);
-              mma_i8<true>(ci_lo[m][n], al[1], bx[n].z, bx[n].w);
+                for (int i = 0; i < 4; ++i)
+                  acc[m][n][i] += (float)(dh[i] * 256 + dl[i]) * ((i & 1) ? f1 : f0);
+              } else {
+                mma_i8<false>(ci_hi[m][n], ah[0], bx[n].x, bx[n].y);
+                mma_i8<true>(ci_lo[m][n], al[0], bx[n].x, bx[n].y);
+                mma_i8<false>(ci_hi[m][n], ah[1], bx[n].z, bx[n].w);
+                mma_i8<true>(ci_lo[m][n], al[1], bx[n].z, bx[n].w);
+              }
             }
           }
         }
@@ -863,6 +873,12 @@ int decode_cb8_down(const DecodeParams& p, int nt, cudaStream_t s) {
 }
 int decode_w8i_logits(const DecodeParams& p, int nt, cudaStream_t s) {
   return launch_cb8_nt<kFmtW8I, 1, kEpiStore, 0>(p, nt, kProfW8Single, s);
+}
+int decode_w8i_gateup(const DecodeParams& p, int nt, cudaStream_t s) {
+  return launch_cb8_nt<kFmtW8I, 2, kEpiSwiglu, 0>(p, nt, kProfW8GateUp, s);
+}
+int decode_w8i_down(const DecodeParams& p, int nt, cudaStream_t s) {
+  return launch_cb8_nt<kFmtW8I, 1, kEpiStore, 1>(p, nt, kProfW8Down, s);
 }
 int decode_cb8_single(const DecodeParams& p, int nt, cudaStream_t s) {
   return cb8_fmt() == kFmtCB8 ? launch_cb8_nt<kFmtCB8, 1, kEpiStore, 0>(p, nt, kProfCb3Single, s)

@@ -56,6 +56,11 @@ int decode_cb8_down(const DecodeParams& p, int nt, cudaStream_t s);
 int decode_cb8_single(const DecodeParams& p, int nt, cudaStream_t s);
 // int8 leaves (W8K, per-output-column scales) times X8 rows, bf16 out: the int8 lm_head (nt: token tiles of 4).
 int decode_w8i_logits(const DecodeParams& p, int nt, cudaStream_t s);
+// The int8 shared expert (W8K leaves, per-output-channel scales) on the int8 MMA: gate/up on X8 rows with the
+// SwiGLU epilogue writing H8 rows, down on those H8 rows storing f32. No dequant arithmetic: the stored leaves are
+// the MMA's A fragments.
+int decode_w8i_gateup(const DecodeParams& p, int nt, cudaStream_t s);
+int decode_w8i_down(const DecodeParams& p, int nt, cudaStream_t s);
 // X8 rows of N bf16 rows of K inputs (K % 256 == 0): x8 [N][K/256][512 B], scale [N].
 int launch_split_x(const uint16_t* x, int N, int K, uint8_t* x8, float* scale, cudaStream_t stream);
 int decode_cb3_gateup(const DecodeParams& p, int nt, cudaStream_t s);

@@ -13,7 +13,7 @@ struct PlanLayoutHost {
 
 // Workspace of the decode path (layout documented at decode_workspace in capi.cu).
 struct DecodeWorkspace {
-  size_t plan, x8, x8s, h, y, hs, ys, done, part_gu, part_dn, part_sgu, part_sdn, total;
+  size_t plan, x8, x8s, h, y, hs, ys, xs8, xs8s, done, part_gu, part_dn, part_sgu, part_sdn, total;
   int cb8;                                    // routed experts on the CB8 (int8-digit) kernels
   int nt, nt_dn;                              // column tiles of the routed gate/up and down kernels
   int nt_s, Rp, P, Ps, RB_gu, RB_dn;
