@@ -308,9 +308,10 @@ int shared_side(const cbmoe_shared* sh, const uint16_t* x, int N, int H, int I, 
   if (W.cb8 && sh->scale_axis == 1 && N <= 8) {
     // int8 MMA on the stored leaves (no dequant arithmetic, so the side stream takes fewer SM cycles from the routed
     // kernels; config 1: CB8 gate+up 102 -> 92 us inside the layer): x split into its own X8 rows here, gate/up ->
-    // SwiGLU -> H8 rows, down -> ys. Whole items only. Up to one 8-token pass: its token tiles hold 4 tokens, so
-    // at 64 tokens it would stream the weights 8 times (measured slower there than the bf16 kernels' 32-token
-    // passes).
+    // SwiGLU -> H8 rows, down -> ys. Whole items only (cutting the 24 gate/up items into pieces over the 48 CTAs
+    // measured slower: 132 us against 93, on the critical path). Up to one 8-token pass: its token tiles hold 4
+    // tokens, so at 64 tokens it would stream the weights 8 times (measured slower there than the bf16 kernels'
+    // 32-token passes).
     uint8_t* xs8 = ws + W.xs8;
     float* xs8s = reinterpret_cast<float*>(ws + W.xs8s);
     uint8_t* hs8 = ws + W.hs;
