@@ -242,11 +242,24 @@ int cbmoe_iq_table_shape(int ggml_type, int* entries, int* width);
 int cbmoe_iq_dequant(int ggml_type, const void* blocks, long long n_blocks, const float* table, float* out,
                      cudaStream_t stream);
 
+/* The int8 tensor-core layout of an IQ2_S or IQ3_S matrix [E][rows][K/256][block bytes] (rows multiple of 64):
+ * an exact load-time transcode (each weight d * k * v as a per-weight code of the signed grid value v, a byte per
+ * group for k, f32 per block for d), which cbmoe_iq_experts_apply uses for that matrix when given. No counterpart
+ * in the reference (its TPU kernel reads the GGUF planes directly). cbmoe_iq8_bytes: size of `out` (0 for other
+ * formats); cbmoe_iq8_build: out 256-byte aligned; synchronizes `stream`; CBMOE_ERR_UNSUPPORTED if the table holds
+ * a grid value the code cannot (IQ2_S: other than 8, 25, 43; IQ3_S: other than the odd values 1..15). */
+size_t cbmoe_iq8_bytes(int ggml_type, int E, int rows, int K);
+int cbmoe_iq8_build(int ggml_type, const void* raw, const float* table, int E, int rows, int K, void* out,
+                    cudaStream_t stream);
+
 /* Routed experts on raw GGUF IQ tables: ResidentFetch.apply with IQ qtypes (resident.py:100-120 over
  * pallas_moe.moe_matvec, pallas_moe.py:238-307), per-matrix formats as in the reference's qtypes. Tables as in
  * the GGUF: [E][rows][K/256][block bytes], gate/up rows = I over K = H, down rows = H over K = I (H, I multiples
- * of 256); tables[] = each matrix's lookup table (see cbmoe_iq_dequant). Computes in fp32 like the reference:
- * g, u = W x, h = swiglu_clamped(g, u, limit), y = sum_k w * (W_down h). y fp32 [N][H], 16-byte aligned. */
+ * of 256); tables[] = each matrix's lookup table (see cbmoe_iq_dequant). g, u = W x, h = swiglu_clamped(g, u,
+ * limit), y = sum_k w * (W_down h), y fp32 [N][H], 16-byte aligned. A matrix with its int8 layout (gate8 / up8 /
+ * down8, from cbmoe_iq8_build; NULL: none) runs on the int8 tensor cores against its input split into two int8
+ * digits per element (exact int32 sums, the input to within 2^-14 of its row's largest); the others compute in
+ * fp32 like the reference. */
 typedef struct {
   int E, H, I;
   int gate_type, up_type, down_type;              /* CBMOE_GGML_IQ2_S / IQ3_S / IQ4_XS / Q2_K / Q3_K */
@@ -256,6 +269,9 @@ typedef struct {
   const float* gate_table;
   const float* up_table;
   const float* down_table;
+  const void* gate8;                              /* cbmoe_iq8_build output of each matrix, or NULL */
+  const void* up8;
+  const void* down8;
 } cbmoe_iq_experts;
 size_t cbmoe_iq_workspace_bytes(const cbmoe_iq_experts* ex, int N, int k);
 int cbmoe_iq_experts_apply(const cbmoe_iq_experts* ex, const uint16_t* x, int N, const int32_t* idx, const float* w,

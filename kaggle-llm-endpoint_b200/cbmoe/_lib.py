@@ -30,7 +30,8 @@ class Shared(ctypes.Structure):
 class IqExperts(ctypes.Structure):
     _fields_ = [("E", c_int), ("H", c_int), ("I", c_int), ("gate_type", c_int), ("up_type", c_int),
                 ("down_type", c_int), ("gate", c_void_p), ("up", c_void_p), ("down", c_void_p),
-                ("gate_table", c_void_p), ("up_table", c_void_p), ("down_table", c_void_p)]
+                ("gate_table", c_void_p), ("up_table", c_void_p), ("down_table", c_void_p),
+                ("gate8", c_void_p), ("up8", c_void_p), ("down8", c_void_p)]
 
 
 # name: (restype, argtypes)
@@ -88,6 +89,8 @@ SIGNATURES = {
     "cbmoe_iq_block_bytes": (c_size_t, [c_int]),
     "cbmoe_iq_table_shape": (c_int, [c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
     "cbmoe_iq_dequant": (c_int, [c_int, c_void_p, ctypes.c_longlong, c_void_p, c_void_p, c_void_p]),
+    "cbmoe_iq8_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "cbmoe_iq8_build": (c_int, [c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "cbmoe_iq_workspace_bytes": (c_size_t, [ctypes.POINTER(IqExperts), c_int, c_int]),
     "cbmoe_iq_experts_apply": (c_int, [ctypes.POINTER(IqExperts), c_void_p, c_int, c_void_p, c_void_p, c_int, c_float,
                                        c_void_p, c_void_p, c_size_t, c_void_p]),

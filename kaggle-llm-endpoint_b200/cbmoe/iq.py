@@ -2,8 +2,10 @@
 the GLM-5.3-Flash tables; Q2_K 84 B and Q3_K 110 B: its MTP layer):
   * dequant_rows: the counterpart of iqquant.dequant_rows (engine/glm53/iqquant.py:230-235) through
     cbmoe_iq_dequant, bit for bit the reference's fp32 values;
-  * pack_layer / apply: routed experts straight from the raw GGUF tables (ResidentFetch.apply with IQ qtypes,
-    resident.py:100-120), through cbmoe_iq_experts_apply, fp32 like the reference's kernel.
+  * pack_layer / apply: routed experts from the GGUF tables (ResidentFetch.apply with IQ qtypes,
+    resident.py:100-120), through cbmoe_iq_experts_apply: IQ2_S and IQ3_S matrices on the int8 tensor cores from
+    an exact load-time transcode (cbmoe_iq8_build), the other formats in fp32 from the raw blocks like the
+    reference's kernel.
 The lookup tables are gguf-py's grids (the reference loads the same ones, iq_grids_data.py), uploaded once per
 device.
 """
@@ -65,10 +67,32 @@ def dequant_rows(raw, qtype, ne0):
     return out.view(-1, ne0)
 
 
-def pack_layer(gate, up, down, qtypes, E, H, I):
+INT8_TYPES = ("IQ2_S", "IQ3_S")   # formats with an int8 tensor-core layout (cbmoe_iq8_build)
+ERR_UNSUPPORTED = -4              # CBMOE_ERR_UNSUPPORTED
+
+
+def build_int8(raw, qtype, E, rows, K):
+    """The int8 tensor-core layout of one matrix (an exact transcode of its raw GGUF blocks), or None when the format
+    has none or its lookup table holds a grid value the layout cannot code."""
+    if qtype not in INT8_TYPES:
+        return None
+    nbytes = lib().cbmoe_iq8_bytes(GGML_TYPE[qtype], E, rows, K)
+    if nbytes == 0:
+        return None
+    out = torch.empty(nbytes, dtype=torch.uint8, device=raw.device)
+    rc = lib().cbmoe_iq8_build(GGML_TYPE[qtype], ptr(raw), ptr(table(qtype, raw.device)), E, rows, K, ptr(out),
+                               stream_handle())
+    if rc == ERR_UNSUPPORTED:   # a grid value the layout cannot code: this matrix stays on the fp32 kernel
+        return None
+    check(rc, "cbmoe_iq8_build")
+    return out
+
+
+def pack_layer(gate, up, down, qtypes, E, H, I, int8=True):
     """Raw GGUF expert tables of one layer on the GPU (uint8, each [E][rows][K/256][block bytes] flattened: gate and
     up I rows over H inputs, down H rows over I inputs) with their formats, qtypes = {"gate_q": "IQ2_S", "up_q":
-    ..., "down_q": ...} (the reference's per-layer qtypes) -> the table dict ResidentFetch.apply takes."""
+    ..., "down_q": ...} (the reference's per-layer qtypes) -> the table dict ResidentFetch.apply takes. int8: also
+    build the int8 tensor-core layout of the IQ2_S / IQ3_S matrices (those then run on the int8 kernels)."""
     require_cuda(gate, up, down)
     assert H % QK_K == 0 and I % QK_K == 0, (H, I)
     mats = {"gate_q": (gate, I, H), "up_q": (up, I, H), "down_q": (down, H, I)}
@@ -77,17 +101,21 @@ def pack_layer(gate, up, down, qtypes, E, H, I):
         assert qt in GGML_TYPE, qt
         assert t.dtype == torch.uint8 and t.numel() == E * rows * (K // QK_K) * block_bytes(qt), \
             (key, qt, t.numel(), E, rows, K)
-    return {"format": "IQ", "E": E, "H": H, "I": I, "qtypes": dict(qtypes),
-            "gate_q": gate.contiguous().view(-1), "up_q": up.contiguous().view(-1), "down_q": down.contiguous().view(-1),
-            "tables": {key: table(qtypes[key], gate.device) for key in mats}}
+    p = {"format": "IQ", "E": E, "H": H, "I": I, "qtypes": dict(qtypes),
+         "gate_q": gate.contiguous().view(-1), "up_q": up.contiguous().view(-1), "down_q": down.contiguous().view(-1),
+         "tables": {key: table(qtypes[key], gate.device) for key in mats}}
+    p["int8"] = {key: (build_int8(p[key], qtypes[key], E, rows, K) if int8 else None)
+                 for key, (_, rows, K) in mats.items()}
+    return p
 
 
 def experts_struct(p):
     q, t = p["qtypes"], p["tables"]
     tp = {k: (None if v is None else v.data_ptr()) for k, v in t.items()}
+    i8 = {k: (None if v is None else v.data_ptr()) for k, v in p.get("int8", {}).items()}
     return IqExperts(p["E"], p["H"], p["I"], GGML_TYPE[q["gate_q"]], GGML_TYPE[q["up_q"]], GGML_TYPE[q["down_q"]],
                      p["gate_q"].data_ptr(), p["up_q"].data_ptr(), p["down_q"].data_ptr(),
-                     tp["gate_q"], tp["up_q"], tp["down_q"])
+                     tp["gate_q"], tp["up_q"], tp["down_q"], i8.get("gate_q"), i8.get("up_q"), i8.get("down_q"))
 
 
 _ws = {}

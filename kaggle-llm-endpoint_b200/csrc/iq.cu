@@ -198,11 +198,16 @@ int launch_iq_matvec(int type, const IqMatParams& p, long long max_items, bool s
   return CBMOE_OK;
 }
 
+// Workspace: plan | g (Rp x I f32) | u | y (Rp x H f32) | X8 rows of x for the gate matrix's int8 kernel (N x H x 2
+// B) and factors | the same for up when its format differs | X8 rows of h for the down matrix's (Rp x I x 2 B) and
+// factors (each X8 region only when that matrix has its int8 layout).
 struct IqWorkspace {
   lyr::PlanLayoutHost L;
   int Rp, P;
-  size_t plan, g, u, y, total;
+  size_t plan, g, u, y, xg8, xg8s, xu8, xu8s, h8, h8s, total;
 };
+
+bool use_iq8(int type, const void* table8) { return table8 != nullptr && iq8_type(type); }
 
 IqWorkspace iq_workspace(const cbmoe_iq_experts* ex, int N, int k) {
   IqWorkspace w;
@@ -213,7 +218,17 @@ IqWorkspace iq_workspace(const cbmoe_iq_experts* ex, int N, int k) {
   w.g = lyr::align_up((size_t)w.L.off[13] * 4);
   w.u = w.g + lyr::align_up((size_t)w.Rp * ex->I * 4);
   w.y = w.u + lyr::align_up((size_t)w.Rp * ex->I * 4);
-  w.total = w.y + lyr::align_up((size_t)w.Rp * ex->H * 4);
+  size_t o = w.y + lyr::align_up((size_t)w.Rp * ex->H * 4);
+  const bool g8 = use_iq8(ex->gate_type, ex->gate8), u8 = use_iq8(ex->up_type, ex->up8);
+  const bool u8_own = u8 && !(g8 && ex->gate_type == ex->up_type);
+  w.xg8 = o;
+  w.xg8s = w.xg8 + (g8 ? lyr::align_up((size_t)N * ex->H * 2) : 0);
+  w.xu8 = w.xg8s + (g8 ? lyr::align_up((size_t)N * 4) : 0);
+  w.xu8s = w.xu8 + (u8_own ? lyr::align_up((size_t)N * ex->H * 2) : 0);
+  w.h8 = w.xu8s + (u8_own ? lyr::align_up((size_t)N * 4) : 0);
+  const bool d8 = use_iq8(ex->down_type, ex->down8);
+  w.h8s = w.h8 + (d8 ? lyr::align_up((size_t)w.Rp * ex->I * 2) : 0);
+  w.total = w.h8s + (d8 ? lyr::align_up((size_t)w.Rp * 4) : 0);
   return w;
 }
 
@@ -224,7 +239,9 @@ bool iq_experts_ok(const cbmoe_iq_experts* ex) {
   return ex && ex->E > 0 && ex->E <= 1024 && ex->H > 0 && ex->I > 0 && ex->H % 256 == 0 && ex->I % 256 == 0 &&
          ok_type(ex->gate_type) && ok_type(ex->up_type) && ok_type(ex->down_type) && ex->gate && ex->up &&
          ex->down && (ex->gate_table || !iq_has_table(ex->gate_type)) &&
-         (ex->up_table || !iq_has_table(ex->up_type)) && (ex->down_table || !iq_has_table(ex->down_type));
+         (ex->up_table || !iq_has_table(ex->up_type)) && (ex->down_table || !iq_has_table(ex->down_type)) &&
+         !(reinterpret_cast<uintptr_t>(ex->gate8) & 255) && !(reinterpret_cast<uintptr_t>(ex->up8) & 255) &&
+         !(reinterpret_cast<uintptr_t>(ex->down8) & 255);
 }
 
 }  // namespace
@@ -267,15 +284,34 @@ extern "C" int cbmoe_iq_experts_apply(const cbmoe_iq_experts* ex, const uint16_t
   p.tok_row = plan + W.L.off[7];
   const long long items_gu = (long long)W.P * ex->I, items_dn = (long long)W.P * ex->H;
   const bool small = (long long)N * k <= 2LL * ex->E;
-  p.w = static_cast<const uint8_t*>(ex->gate);
-  p.table = ex->gate_table;
-  p.out = g;
-  rc = launch_iq_matvec<0>(ex->gate_type, p, items_gu, small, kProfIqGateUp, stream);
+  const int32_t* n_pass = plan + W.L.off[5];
+  // gate and up: the int8 kernels on X8 rows of x where the matrix has its int8 layout, else the fp32 kernel
+  const bool g8 = use_iq8(ex->gate_type, ex->gate8), u8 = use_iq8(ex->up_type, ex->up8);
+  uint8_t* xg8 = ws + W.xg8;
+  float* xg8s = reinterpret_cast<float*>(ws + W.xg8s);
+  uint8_t* xu8 = (g8 && ex->gate_type == ex->up_type) ? xg8 : ws + W.xu8;
+  float* xu8s = (g8 && ex->gate_type == ex->up_type) ? xg8s : reinterpret_cast<float*>(ws + W.xu8s);
+  if (g8) {
+    rc = iq8_split(ex->gate_type, x, false, N, ex->H, xg8, xg8s, stream);
+    if (!rc) rc = iq8_matvec(ex->gate_type, ex->gate8, ex->E, ex->I, ex->H, p.pass_expert, p.pass_row0, p.pass_cnt,
+                             n_pass, p.tok_row, xg8, xg8s, g, kProfIqGateUp, stream);
+  } else {
+    p.w = static_cast<const uint8_t*>(ex->gate);
+    p.table = ex->gate_table;
+    p.out = g;
+    rc = launch_iq_matvec<0>(ex->gate_type, p, items_gu, small, kProfIqGateUp, stream);
+  }
   if (rc) return rc;
-  p.w = static_cast<const uint8_t*>(ex->up);
-  p.table = ex->up_table;
-  p.out = u;
-  rc = launch_iq_matvec<0>(ex->up_type, p, items_gu, small, kProfIqGateUp, stream);
+  if (u8) {
+    if (xu8 != xg8) rc = iq8_split(ex->up_type, x, false, N, ex->H, xu8, xu8s, stream);
+    if (!rc) rc = iq8_matvec(ex->up_type, ex->up8, ex->E, ex->I, ex->H, p.pass_expert, p.pass_row0, p.pass_cnt,
+                             n_pass, p.tok_row, xu8, xu8s, u, kProfIqGateUp, stream);
+  } else {
+    p.w = static_cast<const uint8_t*>(ex->up);
+    p.table = ex->up_table;
+    p.out = u;
+    rc = launch_iq_matvec<0>(ex->up_type, p, items_gu, small, kProfIqGateUp, stream);
+  }
   if (rc) return rc;
   {
     const long long n = (long long)W.Rp * ex->I;
@@ -286,16 +322,24 @@ extern "C" int cbmoe_iq_experts_apply(const cbmoe_iq_experts* ex, const uint16_t
     prof_end(kProfIqGateUp, stream);
     CBMOE_CUDA_TRY(cudaGetLastError());
   }
-  IqMatParams d = p;
-  d.w = static_cast<const uint8_t*>(ex->down);
-  d.table = ex->down_table;
-  d.rows = ex->H;
-  d.K = ex->I;
-  d.x = nullptr;
-  d.tok_row = nullptr;
-  d.h = g;
-  d.out = ys;
-  rc = launch_iq_matvec<1>(ex->down_type, d, items_dn, small, kProfIqDown, stream);
+  if (use_iq8(ex->down_type, ex->down8)) {
+    uint8_t* h8 = ws + W.h8;
+    float* h8s = reinterpret_cast<float*>(ws + W.h8s);
+    rc = iq8_split(ex->down_type, g, true, W.Rp, ex->I, h8, h8s, stream);
+    if (!rc) rc = iq8_matvec(ex->down_type, ex->down8, ex->E, ex->H, ex->I, p.pass_expert, p.pass_row0, p.pass_cnt,
+                             n_pass, nullptr, h8, h8s, ys, kProfIqDown, stream);
+  } else {
+    IqMatParams d = p;
+    d.w = static_cast<const uint8_t*>(ex->down);
+    d.table = ex->down_table;
+    d.rows = ex->H;
+    d.K = ex->I;
+    d.x = nullptr;
+    d.tok_row = nullptr;
+    d.h = g;
+    d.out = ys;
+    rc = launch_iq_matvec<1>(ex->down_type, d, items_dn, small, kProfIqDown, stream);
+  }
   if (rc) return rc;
   return launch_combine(ys, plan + W.L.off[9], w, N, k, ex->H, nullptr, y, nullptr, stream);
 }

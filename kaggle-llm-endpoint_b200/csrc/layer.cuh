@@ -90,4 +90,15 @@ int ep_peer_return(EpPeer* pe, const void* y_sorted, bool bf16, const int32_t* r
 uint16_t* ep_peer_in_x(EpPeer* pe);
 int32_t* ep_peer_in_meta(EpPeer* pe);
 void* ep_peer_in_y(EpPeer* pe);
+
+// Int8 tensor-core kernels of the IQ2_S / IQ3_S expert tables (iq8.cu).
+bool iq8_type(int ggml_type);
+size_t iq8_table_bytes(int ggml_type, int E, int rows, int K);
+// R rows of K inputs (bf16, or f32 when f32) -> X8 rows in ggml_type's storage order + one factor per row.
+int iq8_split(int ggml_type, const void* x, bool f32, int R, int K, uint8_t* x8, float* scale, cudaStream_t s);
+// out[sorted row][rows] = W_e x8[row] over a routing plan's passes (of up to 8 rows); tok_row maps a sorted row to
+// its X8 row (nullptr: itself).
+int iq8_matvec(int ggml_type, const void* table8, int E, int rows, int K, const int32_t* pass_expert,
+               const int32_t* pass_row0, const int32_t* pass_cnt, const int32_t* n_pass, const int32_t* tok_row,
+               const uint8_t* x8, const float* x8_scale, float* out, int kind, cudaStream_t s);
 }  // namespace cbmoe

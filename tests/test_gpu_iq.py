@@ -91,6 +91,55 @@ def test_iq_experts_apply(cbmoe, types, N, k, E):
     assert cbmoe.device_errors(clear=True) == 0
 
 
+@pytest.mark.parametrize("types", [("IQ2_S", "IQ2_S", "IQ3_S"), ("IQ3_S", "IQ2_S", "IQ2_S"),
+                                   ("IQ2_S", "IQ4_XS", "IQ3_S")])
+@pytest.mark.parametrize("N,k,E", [(1, 8, 16), (8, 8, 24), (37, 4, 8), (64, 8, 8)])
+def test_iq_int8_layout_against_fp32_kernels(cbmoe, types, N, k, E):
+    """The IQ2_S / IQ3_S matrices on the int8 tensor-core layout (exact transcode, X8 activations) against the same
+    layer on the fp32 kernels and against the oracle; passes of 1-8 tokens (N = 64, E = 8: 64 slots per expert)."""
+    from oracle import gen, moe
+    H, I = 512, 256
+    rng = np.random.default_rng(N * 7 + E + len("".join(types)))
+    qtypes = dict(zip(("gate_q", "up_q", "down_q"), types))
+    shapes = {"gate_q": (I, H), "up_q": (I, H), "down_q": (H, I)}
+    raw = {key: oiq.random_blocks(rng, E * rows * (K // 256), qtypes[key]) for key, (rows, K) in shapes.items()}
+    dev = {key: torch.from_numpy(b.reshape(-1)).cuda() for key, b in raw.items()}
+    p8 = cbmoe.iq.pack_layer(dev["gate_q"], dev["up_q"], dev["down_q"], qtypes, E, H, I)
+    p32 = cbmoe.iq.pack_layer(dev["gate_q"], dev["up_q"], dev["down_q"], qtypes, E, H, I, int8=False)
+    for key in shapes:
+        assert (p8["int8"][key] is not None) == (qtypes[key] in ("IQ2_S", "IQ3_S"))
+    x = gen.activations(rng, N, H)
+    idx, w = gen.routing(rng, N, E, k)
+    xt = torch.from_numpy(x.view(np.uint16).copy()).cuda().view(torch.bfloat16)
+    it, wt = torch.from_numpy(idx).cuda(), torch.from_numpy(w).cuda()
+    y8 = cbmoe.iq.apply(p8, xt, it, wt, gen.LIMIT)
+    y32 = cbmoe.iq.apply(p32, xt, it, wt, gen.LIMIT)
+    tabs = oiq.tables()
+    W = {key: oiq.experts_dense(raw[key], qtypes[key], E, rows, K, tabs) for key, (rows, K) in shapes.items()}
+    want = oiq.decode_apply(x.astype(np.float32), idx, w, W["gate_q"], W["up_q"], W["down_q"], gen.LIMIT)
+    assert moe.max_rel_err(y8.cpu().numpy(), want) < 2e-3
+    assert moe.max_rel_err(y8.cpu().numpy(), y32.cpu().numpy()) < 2e-3
+    assert cbmoe.device_errors(clear=True) == 0
+
+
+def test_iq8_build_rejects_bad_arguments(cbmoe):
+    L = cbmoe.lib()
+    from cbmoe._lib import ptr, stream_handle
+    assert L.cbmoe_iq8_bytes(23, 2, 64, 256) == 0                   # IQ4_XS: no int8 layout
+    assert L.cbmoe_iq8_bytes(22, 2, 48, 256) == 0                   # rows not a multiple of 64
+    n = L.cbmoe_iq8_bytes(22, 2, 64, 256)
+    assert n > 0
+    raw = torch.zeros(2 * 64 * 82, dtype=torch.uint8, device="cuda")
+    out = torch.empty(n, dtype=torch.uint8, device="cuda")
+    tab = cbmoe.iq.table("IQ2_S", raw.device)
+    assert L.cbmoe_iq8_build(23, ptr(raw), ptr(tab), 2, 64, 256, ptr(out), stream_handle()) == -4
+    assert L.cbmoe_iq8_build(22, ptr(raw), ptr(tab), 2, 48, 256, ptr(out), stream_handle()) == -1
+    bad = tab.clone()
+    bad[5] = 7.0                                                      # not a value the 3-bit code holds
+    assert L.cbmoe_iq8_build(22, ptr(raw), ptr(bad), 2, 64, 256, ptr(out), stream_handle()) == -4
+    assert L.cbmoe_iq8_build(22, ptr(raw), ptr(tab), 2, 64, 256, ptr(out), stream_handle()) == 0
+
+
 def test_iq_qtypes_mismatch_raises(cbmoe):
     E, H, I = 2, 256, 256
     qtypes = {"gate_q": "IQ3_S", "up_q": "IQ3_S", "down_q": "IQ3_S"}
