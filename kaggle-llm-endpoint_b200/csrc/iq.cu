@@ -313,7 +313,14 @@ extern "C" int cbmoe_iq_experts_apply(const cbmoe_iq_experts* ex, const uint16_t
     rc = launch_iq_matvec<0>(ex->up_type, p, items_gu, small, kProfIqGateUp, stream);
   }
   if (rc) return rc;
-  {
+  if (use_iq8(ex->down_type, ex->down8)) {
+    // SwiGLU and the split of h into X8 digits in one pass over the rows (h itself is not stored)
+    uint8_t* h8 = ws + W.h8;
+    float* h8s = reinterpret_cast<float*>(ws + W.h8s);
+    rc = iq8_swiglu_split(ex->down_type, g, u, limit, W.Rp, ex->I, h8, h8s, stream);
+    if (!rc) rc = iq8_matvec(ex->down_type, ex->down8, ex->E, ex->H, ex->I, p.pass_expert, p.pass_row0, p.pass_cnt,
+                             n_pass, nullptr, h8, h8s, ys, kProfIqDown, stream);
+  } else {
     const long long n = (long long)W.Rp * ex->I;
     long long blocks = (n + 255) / 256;
     if (blocks > (long long)num_sms() * 8) blocks = (long long)num_sms() * 8;
@@ -321,14 +328,6 @@ extern "C" int cbmoe_iq_experts_apply(const cbmoe_iq_experts* ex, const uint16_t
     iq_swiglu_kernel<<<(int)blocks, 256, 0, stream>>>(g, u, n, limit);
     prof_end(kProfIqGateUp, stream);
     CBMOE_CUDA_TRY(cudaGetLastError());
-  }
-  if (use_iq8(ex->down_type, ex->down8)) {
-    uint8_t* h8 = ws + W.h8;
-    float* h8s = reinterpret_cast<float*>(ws + W.h8s);
-    rc = iq8_split(ex->down_type, g, true, W.Rp, ex->I, h8, h8s, stream);
-    if (!rc) rc = iq8_matvec(ex->down_type, ex->down8, ex->E, ex->H, ex->I, p.pass_expert, p.pass_row0, p.pass_cnt,
-                             n_pass, nullptr, h8, h8s, ys, kProfIqDown, stream);
-  } else {
     IqMatParams d = p;
     d.w = static_cast<const uint8_t*>(ex->down);
     d.table = ex->down_table;

@@ -41,7 +41,8 @@ __global__ void iq8_units_kernel(const uint8_t* __restrict__ raw, const float* _
     const bool ok = iq8_lane_words<T>(bg, bh, table, lane, words);
     uint4* dst = reinterpret_cast<uint4*>(units + ((size_t)wi * 32 + lane) * LW);
 #pragma unroll
-    for (int i = 0; i < LW / 4; ++i) dst[i] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
+    for (int i = 0; i < LW / 4; ++i)
+      dst[i] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
     if (!ok) atomicOr(bad, 1);
   }
 }
@@ -64,13 +65,17 @@ __global__ void iq8_scales_kernel(const uint8_t* __restrict__ raw, long long n_b
 // d0 = X - 256 d1, factor 2^-t; stored per stage as [chunk 4][digit 2][64], storage byte s of a chunk's plane
 // holding input iq8_perm<T>(s). Rows without a finite maximum (padding rows of the routing plan) get factor 1 and
 // clamped digits; no pass reads them.
-template <int T, bool F32>
-__global__ void __launch_bounds__(256) iq8_split_kernel(const void* __restrict__ x, int R, int K,
-                                                        uint8_t* __restrict__ x8, float* __restrict__ scale) {
+// IN: 0 = bf16 rows x, 1 = f32 rows x, 2 = swiglu_clamped(x, u, limit) of f32 rows x (gate) and u (up).
+template <int T, int IN>
+__global__ void __launch_bounds__(256) iq8_split_kernel(const void* __restrict__ x, const float* __restrict__ u,
+                                                        float limit, int R, int K, uint8_t* __restrict__ x8,
+                                                        float* __restrict__ scale) {
   __shared__ float red[8];
   for (int r = blockIdx.x; r < R; r += gridDim.x) {
     auto val = [&](int i) -> float {
-      if constexpr (F32) return static_cast<const float*>(x)[(size_t)r * K + i];
+      if constexpr (IN == 1) return static_cast<const float*>(x)[(size_t)r * K + i];
+      else if constexpr (IN == 2)
+        return swiglu_clamped(static_cast<const float*>(x)[(size_t)r * K + i], u[(size_t)r * K + i], limit);
       else return __uint_as_float((uint32_t)static_cast<const uint16_t*>(x)[(size_t)r * K + i] << 16);
     };
     float mx = 0.f;
@@ -206,7 +211,8 @@ __global__ void __launch_bounds__(128, 4) iq8_matvec_kernel(const Iq8Params p) {
         uint4 bx[NT];
 #pragma unroll
         for (int n = 0; n < NT; ++n)
-          if (n == 0 || n * 4 < cnt) bx[n] = __ldg(reinterpret_cast<const uint4*>(bsrc[n] + ks * kX8StageBytes + c * 128));
+          if (n == 0 || n * 4 < cnt)
+            bx[n] = __ldg(reinterpret_cast<const uint4*>(bsrc[n] + ks * kX8StageBytes + c * 128));
         if constexpr (T == CBMOE_GGML_IQ2_S) {
           uint32_t ag[4], ah[4];
           iq8_frag_iq2(cur.w[3 * c], cur.w[3 * c + 1], cur.w[3 * c + 2], ag, ah);
@@ -282,12 +288,14 @@ int launch_iq8_matvec(const Iq8Params& p, int kind, cudaStream_t s) {
 }
 
 template <int T>
-int launch_iq8_split(const void* x, bool f32, int R, int K, uint8_t* x8, float* scale, cudaStream_t s) {
+int launch_iq8_split(const void* x, const float* u, float limit, int in, int R, int K, uint8_t* x8, float* scale,
+                     cudaStream_t s) {
   if (R <= 0) return CBMOE_OK;
   const int blocks = R < num_sms() * 4 ? R : num_sms() * 4;
   prof_begin(kProfOther, s);
-  if (f32) iq8_split_kernel<T, true><<<blocks, 256, 0, s>>>(x, R, K, x8, scale);
-  else iq8_split_kernel<T, false><<<blocks, 256, 0, s>>>(x, R, K, x8, scale);
+  if (in == 1) iq8_split_kernel<T, 1><<<blocks, 256, 0, s>>>(x, u, limit, R, K, x8, scale);
+  else if (in == 2) iq8_split_kernel<T, 2><<<blocks, 256, 0, s>>>(x, u, limit, R, K, x8, scale);
+  else iq8_split_kernel<T, 0><<<blocks, 256, 0, s>>>(x, u, limit, R, K, x8, scale);
   prof_end(kProfOther, s);
   CBMOE_CUDA_TRY(cudaGetLastError());
   return CBMOE_OK;
@@ -336,8 +344,14 @@ size_t iq8_table_bytes(int t, int E, int rows, int K) {
 }
 
 int iq8_split(int t, const void* x, bool f32, int R, int K, uint8_t* x8, float* scale, cudaStream_t s) {
-  return t == CBMOE_GGML_IQ2_S ? launch_iq8_split<CBMOE_GGML_IQ2_S>(x, f32, R, K, x8, scale, s)
-                               : launch_iq8_split<CBMOE_GGML_IQ3_S>(x, f32, R, K, x8, scale, s);
+  return t == CBMOE_GGML_IQ2_S ? launch_iq8_split<CBMOE_GGML_IQ2_S>(x, nullptr, 0.f, f32 ? 1 : 0, R, K, x8, scale, s)
+                               : launch_iq8_split<CBMOE_GGML_IQ3_S>(x, nullptr, 0.f, f32 ? 1 : 0, R, K, x8, scale, s);
+}
+
+int iq8_swiglu_split(int t, const float* g, const float* u, float limit, int R, int K, uint8_t* x8, float* scale,
+                     cudaStream_t s) {
+  return t == CBMOE_GGML_IQ2_S ? launch_iq8_split<CBMOE_GGML_IQ2_S>(g, u, limit, 2, R, K, x8, scale, s)
+                               : launch_iq8_split<CBMOE_GGML_IQ3_S>(g, u, limit, 2, R, K, x8, scale, s);
 }
 
 int iq8_matvec(int t, const void* table8, int E, int rows, int K, const int32_t* plan_pass_expert,

@@ -96,6 +96,9 @@ bool iq8_type(int ggml_type);
 size_t iq8_table_bytes(int ggml_type, int E, int rows, int K);
 // R rows of K inputs (bf16, or f32 when f32) -> X8 rows in ggml_type's storage order + one factor per row.
 int iq8_split(int ggml_type, const void* x, bool f32, int R, int K, uint8_t* x8, float* scale, cudaStream_t s);
+// The same for h = swiglu_clamped(g, u, limit) of f32 rows g, u (h itself is not stored).
+int iq8_swiglu_split(int ggml_type, const float* g, const float* u, float limit, int R, int K, uint8_t* x8,
+                     float* scale, cudaStream_t s);
 // out[sorted row][rows] = W_e x8[row] over a routing plan's passes (of up to 8 rows); tok_row maps a sorted row to
 // its X8 row (nullptr: itself).
 int iq8_matvec(int ggml_type, const void* table8, int E, int rows, int K, const int32_t* pass_expert,
