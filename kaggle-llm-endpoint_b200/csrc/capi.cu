@@ -129,7 +129,6 @@ bool has_cb8(const cbmoe_experts* ex) { return ex->gateup_cb8 != nullptr && ex->
 DecodeParams base_params() {
   DecodeParams p{};
   p.E = 1;
-  p.sel = {0xffffffffu, 1u << 16, 1u << 29, 1u << 30, 1u << 31};
   return p;
 }
 

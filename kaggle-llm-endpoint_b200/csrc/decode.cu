@@ -16,11 +16,8 @@
 
 namespace cbmoe {
 
-// CB8 kernels come in two builds of the selector arithmetic: kFmtCB8 (part of it as multiply-adds on the FMA pipe,
-// CBMOE_CB8_FMA_MODE of cb8_dequant_chunk) and kFmtCB8A (shifts and masks on the ALU pipe).
-#ifndef CBMOE_CB8_FMA_MODE
-#define CBMOE_CB8_FMA_MODE 2
-#endif
+// The CB8 kernels' template format value (kFmtCB8 is the tables' format id; the kernels are built once, with the
+// selector arithmetic on the ALU pipe).
 constexpr int kFmtCB8A = 3;
 template <>
 struct Fmt<kFmtCB8A> {
@@ -583,9 +580,7 @@ __global__ void __launch_bounds__(kDecodeThreads, decode_min_blocks<FMT, NT, HIL
               }
             }
           } else {
-            cb8_dequant_chunk<FMT == kFmtCB8 ? CBMOE_CB8_FMA_MODE : 0>(wd[m][3 * c], wd[m][3 * c + 1],
-                                                                        wd[m][3 * c + 2], c8g[m], c8h[m], p.sel, ah,
-                                                                        al);
+            cb8_dequant_chunk(wd[m][3 * c], wd[m][3 * c + 1], wd[m][3 * c + 2], c8g[m], c8h[m], ah, al);
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
               if (!(n == 0 || n * SM::kTokPerTile < h.cnt)) continue;
@@ -837,20 +832,6 @@ int launch_combine(const float* y_sorted, const int* row_slot, const float* wts,
 #ifndef CBMOE_STAGES_CB8_H8
 #define CBMOE_STAGES_CB8_H8 4
 #endif
-#ifndef CBMOE_CB8_SEL_FMA
-#define CBMOE_CB8_SEL_FMA 0
-#endif
-// Selector arithmetic of the CB8 kernels: on the ALU pipe (default: shorter dependency latency, measured faster)
-// or on the FMA pipe (CBMOE_CB8_SEL=fma in the environment, read once: a measurement switch).
-static int cb8_fmt() {
-  static int f = -1;
-  if (f < 0) {
-    const char* e = getenv("CBMOE_CB8_SEL");
-    f = (e && e[0] == 'f') ? kFmtCB8 : (e && e[0] == 'a') ? kFmtCB8A : (CBMOE_CB8_SEL_FMA ? kFmtCB8 : kFmtCB8A);
-  }
-  return f;
-}
-
 template <int FMT, int NMAT, int EPI, int HILO>
 int launch_cb8_nt(const DecodeParams& p, int nt, int kind, cudaStream_t stream) {
   constexpr int NS = HILO ? CBMOE_STAGES_CB8_H8 : CBMOE_STAGES_CB8_X8;
@@ -864,12 +845,10 @@ int launch_cb8_nt(const DecodeParams& p, int nt, int kind, cudaStream_t stream) 
 }
 
 int decode_cb8_gateup(const DecodeParams& p, int nt, cudaStream_t s) {
-  return cb8_fmt() == kFmtCB8 ? launch_cb8_nt<kFmtCB8, 2, kEpiSwiglu, 0>(p, nt, kProfCb3GateUp, s)
-                              : launch_cb8_nt<kFmtCB8A, 2, kEpiSwiglu, 0>(p, nt, kProfCb3GateUp, s);
+  return launch_cb8_nt<kFmtCB8A, 2, kEpiSwiglu, 0>(p, nt, kProfCb3GateUp, s);
 }
 int decode_cb8_down(const DecodeParams& p, int nt, cudaStream_t s) {
-  return cb8_fmt() == kFmtCB8 ? launch_cb8_nt<kFmtCB8, 1, kEpiStore, 1>(p, nt, kProfCb3Down, s)
-                              : launch_cb8_nt<kFmtCB8A, 1, kEpiStore, 1>(p, nt, kProfCb3Down, s);
+  return launch_cb8_nt<kFmtCB8A, 1, kEpiStore, 1>(p, nt, kProfCb3Down, s);
 }
 int decode_w8i_logits(const DecodeParams& p, int nt, cudaStream_t s) {
   return launch_cb8_nt<kFmtW8I, 1, kEpiStore, 0>(p, nt, kProfW8Single, s);
@@ -881,8 +860,7 @@ int decode_w8i_down(const DecodeParams& p, int nt, cudaStream_t s) {
   return launch_cb8_nt<kFmtW8I, 1, kEpiStore, 1>(p, nt, kProfW8Down, s);
 }
 int decode_cb8_single(const DecodeParams& p, int nt, cudaStream_t s) {
-  return cb8_fmt() == kFmtCB8 ? launch_cb8_nt<kFmtCB8, 1, kEpiStore, 0>(p, nt, kProfCb3Single, s)
-                              : launch_cb8_nt<kFmtCB8A, 1, kEpiStore, 0>(p, nt, kProfCb3Single, s);
+  return launch_cb8_nt<kFmtCB8A, 1, kEpiStore, 0>(p, nt, kProfCb3Single, s);
 }
 
 __global__ void split_x_kernel(const uint16_t* __restrict__ x, int N, int K, uint8_t* __restrict__ x8,

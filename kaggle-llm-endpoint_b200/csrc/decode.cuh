@@ -13,7 +13,6 @@ struct DecodeParams {
   const uint8_t* wq;        // weights in unit layout (CB3K index bits or W8K int8)
   const uint32_t* cb;       // CB3K codebooks
   const uint8_t* cb8;       // CB8 tables + row factors (layout.cuh)
-  SelConst sel;             // CB8 selector operands (base_params)
   const float* s0;          // W8K scales, matrix 0 / 1
   const float* s1;
   int scale_axis;

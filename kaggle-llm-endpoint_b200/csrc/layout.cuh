@@ -90,62 +90,17 @@ struct Cb8 {
   uint32_t ha, hb, la, lb;
 };
 
-// Operands the selector arithmetic takes from the kernel parameters, so that it compiles to integer multiply-adds
-// (FMA pipe) rather than shifts and masks (ALU pipe, which the table lookups keep busy): -1, 2^16, 2^29, 2^30, 2^31.
-struct SelConst {
-  uint32_t m1, s16, s29, s30, s31;
-};
-
-__device__ __forceinline__ uint32_t mul_hi(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-__device__ __forceinline__ uint32_t mad_hi(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t d;
-  asm("mad.hi.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-__device__ __forceinline__ uint32_t mad_lo(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t d;
-  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-
 // One chunk of one CB8 matrix: the 3 CB3K index words of this lane -> int8 A fragments of the hi and lo bytes for
 // the chunk's two k32 MMA steps: ah[h] / al[h] = {row g group 2h, row g+8 group 2h, row g group 2h+1, row g+8
-// group 2h+1}. Selectors as cb3k_dequant_chunk; the spare-bit word and the upper halves come from multiply-adds:
-// w - (w & 0x77777777) = the spare bits, mul.hi by 2^(32-n) = a right shift by n.
-// kSel: 0 = every selector operation on the ALU pipe; 1 = the spare-bit word and the upper halves on the FMA pipe
-// (multiply-adds); 2 = only the upper halves (4 independent multiply-highs) on the FMA pipe.
-template <int kSel>
+// group 2h+1}. Selectors as cb3k_dequant_chunk (shifts and masks; moving the spare-bit word and the upper halves to
+// multiply-adds on the FMA pipe measured slower).
 __device__ __forceinline__ void cb8_dequant_chunk(uint32_t w0, uint32_t w1, uint32_t w2, const Cb8& cg,
-                                                  const Cb8& ch, const SelConst& k, uint32_t (&ah)[2][4],
-                                                  uint32_t (&al)[2][4]) {
+                                                  const Cb8& ch, uint32_t (&ah)[2][4], uint32_t (&al)[2][4]) {
   const uint32_t g01 = w0 & 0x77777777u;
   const uint32_t g23 = w1 & 0x77777777u;
   const uint32_t h01 = w2 & 0x77777777u;
-  uint32_t h23, g01u, g23u, h01u, h23u;
-  if constexpr (kSel == 1) {
-    const uint32_t s0 = mad_lo(g01, k.m1, w0), s1 = mad_lo(g23, k.m1, w1), s2 = mad_lo(h01, k.m1, w2);
-    h23 = mad_hi(s0, k.s29, mad_hi(s1, k.s30, mul_hi(s2, k.s31)));
-    g01u = mul_hi(g01, k.s16);
-    g23u = mul_hi(g23, k.s16);
-    h01u = mul_hi(h01, k.s16);
-    h23u = mul_hi(h23, k.s16);
-  } else if constexpr (kSel == 2) {
-    h23 = ((w0 >> 3) & 0x11111111u) | ((w1 >> 2) & 0x22222222u) | ((w2 >> 1) & 0x44444444u);
-    g01u = mul_hi(g01, k.s16);
-    g23u = mul_hi(g23, k.s16);
-    h01u = mul_hi(h01, k.s16);
-    h23u = mul_hi(h23, k.s16);
-  } else {
-    h23 = ((w0 >> 3) & 0x11111111u) | ((w1 >> 2) & 0x22222222u) | ((w2 >> 1) & 0x44444444u);
-    g01u = g01 >> 16;
-    g23u = g23 >> 16;
-    h01u = h01 >> 16;
-    h23u = h23 >> 16;
-  }
+  const uint32_t h23 = ((w0 >> 3) & 0x11111111u) | ((w1 >> 2) & 0x22222222u) | ((w2 >> 1) & 0x44444444u);
+  const uint32_t g01u = g01 >> 16, g23u = g23 >> 16, h01u = h01 >> 16, h23u = h23 >> 16;
   ah[0][0] = prmt(cg.ha, cg.hb, g01);
   ah[0][1] = prmt(ch.ha, ch.hb, h01);
   ah[0][2] = prmt(cg.ha, cg.hb, g01u);
