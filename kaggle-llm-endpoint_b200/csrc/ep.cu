@@ -109,7 +109,9 @@ EpWorkspace ep_workspace(int E_loc, int H, int I, int N_local, int k, int nranks
   w.y_recv = w.ones + align_up((size_t)w.R * 4);
   w.y_back = w.y_recv + align_up((size_t)w.R * H * 4);
   w.sub_local = w.y_back + align_up((size_t)w.R * H * 4);
-  w.Wl = lyr::decode_workspace(E_loc, H, I, N_local, k, -1, 0);   // shared-expert regions only
+  // shared-expert regions only; with CB8 tables a one-pass batch (<= 8 local tokens) gets the int8-MMA shared
+  // expert, as on one GPU
+  w.Wl = lyr::decode_workspace(E_loc, H, I, N_local, k, -1, cb8);
   w.sub_recv = w.sub_local + align_up(w.Wl.total);
   // The receive buffer holds up to R rows, but a rank expects about its own slot count (N_local * k) of real
   // ones: AUTO chooses the kernels by that. From 8 rows per local expert on, the tensor-core GEMMs, except where
