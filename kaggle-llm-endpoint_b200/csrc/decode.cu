@@ -2,15 +2,19 @@
 //
 // Counterpart of the reference's moe_matvec Pallas kernel (pallas_moe.py:238-307) and of `_apply_kernel`'s
 // gate/up -> swiglu -> down composition (resident.py:110-120), with two changes of design for B200:
-//   * work is per (expert pass, 64-row block), not per slot: a pass is up to 8*NT tokens routed to one expert, so
-//     an expert's weights stream from HBM once per pass instead of once per (token, slot) pair;
+//   * work is per (expert pass, 64-row block), not per slot: a pass is a few tokens routed to one expert, so an
+//     expert's weights stream from HBM once per pass instead of once per (token, slot) pair;
 //   * the weights never leave registers in dense form: a producer warp streams 256-input stages of packed bits
 //     into shared memory with bulk async copies (mbarrier pipeline, NSTAGE deep); four consumer warps turn them
-//     into bf16 tensor-core fragments with byte permutes (CB3K) or int8 -> fp32 * scale -> bf16 (W8K) and
-//     multiply them with mma.sync m16n8k16 against the pass's tokens, accumulating in fp32.
-// Persistent grid: gridDim = SMs x resident CTAs, each streaming an equal share of all items' stages (stream-K).
-// Epilogues: SWIGLU (gate+up -> h stored as bf16 hi + bf16 lo, so the down matvec sees h to ~16 mantissa bits),
-// STORE (fp32 rows). The layer's weighted sum of the slots (+ the shared expert) is combine_kernel.
+//     into tensor-core fragments in registers and multiply them against the pass's tokens:
+//       CB8 (default for CB3 layers): byte-table lookups into int8 hi / lo digits of the 16-bit fixed-point
+//         codebook, mma.sync m16n8k32 int8 against X8 (gate/up) or H8 (down) activation digits, exact int32 sums;
+//       W8I: the stored int8 leaves as the int8 A fragments (the shared expert at small batches, the int8 lm_head);
+//       CB3 / W8: bf16 fragments (byte permutes of the bf16 codebooks; int8 -> fp32 * scale -> bf16) and
+//         mma.sync m16n8k16 bf16, fp32 accumulation (layers without CB8 tables, or many tokens per expert).
+// Persistent grid: gridDim = SMs x resident CTAs, work handed out by tickets, the last partial wave of long items
+// cut into pieces. Epilogues: SWIGLU (gate+up -> h as H8 digit rows, or bf16 hi + lo), STORE (f32 or bf16 rows).
+// The layer's weighted sum of the slots (+ the shared expert) is combine_kernel.
 #include "decode.cuh"
 #include "profile.cuh"
 
